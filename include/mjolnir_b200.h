@@ -1,0 +1,166 @@
+/*
+ * mjolnir_b200 -- C ABI of the B200 (sm_100a) decode-attention hot path.
+ *
+ * Three device operations behind plain pointers, sizes and a cudaStream_t
+ * passed as void*. No torch types, no allocation inside any call (the caller
+ * owns every buffer, including the split-KV scratch), every call returns an
+ * int status (MJ_OK = 0) and never aborts the process.
+ *
+ *   mj_cache_write  quantize-on-write of new K/V rows into the paged cache
+ *                   (fp8-e4m3, or e2m3 packed 4 codes per 3 bytes)
+ *   mj_decode       paged split-KV decode attention over that cache
+ *   mj_combine      log-sum-exp merge of the split-KV partials
+ *
+ * Reference interfaces these replace (GoBrrr-ai/mjolnir, src/mjolnir/mjolnir/):
+ *   mj_cache_write  kvfp6.py:218-254 `write_kv` (e2m3) and the fp8 write
+ *                   `MjolnirImpl.do_kv_cache_update` -> vLLM
+ *                   `reshape_and_cache_flash` (backend.py:474-483)
+ *   mj_decode       arch/thor/runner.py:374-407 `T5DecodeRunner._launch`, the
+ *                   compiled `decode` kernel (arch/thor/decode.py:243-1471,
+ *                   launched by arch/thor/call.py:481-529)
+ *   mj_combine      the `reduction` kernel (arch/thor/decode.py:1473-1541,
+ *                   launched by arch/thor/call.py:536-560)
+ *
+ * Layout conventions
+ *   Q / O        (tokens, h_q, head_size), token = seq * q_len + qi, head dim
+ *                contiguous; token and head strides in ELEMENTS.
+ *   K / V cache  logical views (num_pages, page_size, h_k, row_bytes) with the
+ *                row (head_size elements, or head_size*3/4 packed e2m3 bytes)
+ *                contiguous; page / row / head strides in BYTES (any physical
+ *                layout: vLLM's (B, H, N, 2*row), FlashInfer NHD/HND, ...).
+ *   block_table  int32 (>= num_seqs, block_table_stride); token t of sequence s
+ *                lives in page block_table[s * stride + t / page_size].
+ *   seq_lens     int32 (num_seqs,), INCLUDING the step's q_len new tokens.
+ *   work         int32 (num_work, 4): (seq, tile_begin, tile_end, split) in
+ *                128-row KV tiles; tile_begin == tile_end is an empty item.
+ *   n_splits     int32 (num_seqs,): number of work items of each sequence.
+ */
+#ifndef MJOLNIR_B200_H
+#define MJOLNIR_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MJ_ABI_VERSION 1
+
+/* status codes */
+#define MJ_OK 0
+#define MJ_ERR_INVALID 1     /* an argument failed validation (see mj_last_error) */
+#define MJ_ERR_UNSUPPORTED 2 /* a shape / format / alignment this build does not run */
+#define MJ_ERR_CUDA 3        /* a CUDA runtime call failed (see mj_last_error) */
+#define MJ_ERR_DEVICE 4      /* a kernel flagged a bad index in the device status word */
+
+/* device status word codes (written by kernels into args->status, if given) */
+#define MJ_DEV_OK 0
+#define MJ_DEV_BAD_PAGE 1    /* block-table entry or slot page outside [0, num_pages) */
+#define MJ_DEV_BAD_SPLIT 2   /* work item split >= max_splits or seq >= part_seqs */
+#define MJ_DEV_TIMEOUT 3     /* a bounded wait in a pipelined kernel gave up */
+
+/* KV formats */
+#define MJ_KV_FP8_E4M3 0
+#define MJ_KV_E2M3 1
+
+/* element types of Q / O / new K,V rows */
+#define MJ_DT_BF16 0
+#define MJ_DT_FP16 1
+#define MJ_DT_FP32 2
+
+/* scale / descale modes */
+#define MJ_SCALE_TENSOR 0   /* one fp32 */
+#define MJ_SCALE_HEAD 1     /* (h_k,) fp32 */
+#define MJ_SCALE_CHANNEL 2  /* (h_k, head_size) fp32 -- cache write only */
+#define MJ_SCALE_SEQ_HEAD 3 /* (num_seqs, h_k) fp32 -- decode descales only */
+
+/* Last error message of the calling thread ("" when none). */
+const char* mj_last_error(void);
+/* MJ_ABI_VERSION of the loaded library. */
+int mj_abi_version(void);
+/* Bytes of one K (or V) row: head_size (fp8) or head_size*3/4 (e2m3); -1 if invalid. */
+int mj_row_bytes(int head_size, int kv_format);
+
+/* ------------------------------------------------------------------------ */
+/* Quantize-on-write (reshape_and_cache).                                   */
+/* Replaces kvfp6.py:218-254 write_kv and the fp8 reshape_and_cache_flash    */
+/* call of backend.py:474-483. Token t with slot_mapping[t] >= 0 is written  */
+/* to page slot / page_size, row slot % page_size; slot < 0 is skipped.      */
+/* e2m3: x / scale in fp32 (IEEE division), round to nearest with ties to   */
+/* the smaller magnitude, saturate at 7.5, no -0; codes packed little-endian */
+/* (c0 | c1<<6 | c2<<12 | c3<<18 -> 3 bytes) -- quant.py:34-65.              */
+/* fp8: x / scale in fp32, round to nearest even, saturate at +-448.         */
+typedef struct mj_cache_write_args {
+  const void* key;              /* (num_tokens, h_k, head_size), head dim contiguous */
+  const void* value;
+  int src_dtype;                /* MJ_DT_BF16 | MJ_DT_FP16 | MJ_DT_FP32 */
+  int64_t num_tokens;
+  int h_k;
+  int head_size;                /* multiple of 16 */
+  int64_t key_stride_tok, key_stride_head;     /* elements */
+  int64_t value_stride_tok, value_stride_head; /* elements */
+  void* k_cache;                /* logical (num_pages, page_size, h_k, row_bytes) */
+  void* v_cache;
+  int64_t k_stride_page, k_stride_row, k_stride_head; /* bytes */
+  int64_t v_stride_page, v_stride_row, v_stride_head; /* bytes */
+  int64_t num_pages;
+  int page_size;
+  int kv_format;                /* MJ_KV_FP8_E4M3 | MJ_KV_E2M3 */
+  const int64_t* slot_mapping;  /* (num_tokens,) */
+  const float* k_scale;         /* per k_scale_mode */
+  int k_scale_mode;             /* MJ_SCALE_TENSOR | _HEAD | _CHANNEL */
+  const float* v_scale;
+  int v_scale_mode;
+  int32_t* status;              /* optional device status word (MJ_DEV_*) */
+} mj_cache_write_args;
+
+int mj_cache_write(const mj_cache_write_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Paged split-KV decode attention.                                          */
+/* Query row n = qi * h_r + r of KV head h (h_r = h_q / h_k) reads token     */
+/* seq * q_len + qi, q head h * h_r + r. With causal != 0, query token qi of */
+/* a sequence of length L sees keys 0 .. L - q_len + qi, otherwise all L.    */
+/* score = (q * q_mul) . k_code * softmax_scale * k_descale;                 */
+/* O = softmax(score) . v_code * v_descale * o_mul. A row that sees no key   */
+/* gets O = 0 and LSE = -inf.                                                 */
+/* A work item whose sequence has n_splits == 1 writes the final O (and LSE);*/
+/* otherwise it writes its chunk-normalized partial into o_part / lse_part   */
+/* at [split][seq][h][n], merged by mj_combine (or by mj_decode itself when  */
+/* with_combine != 0). No allocation: safe inside CUDA-graph capture.        */
+typedef struct mj_decode_args {
+  int num_seqs, q_len, h_q, h_k, head_size, page_size, kv_format;
+  const void* q; int q_dtype; int64_t q_stride_tok, q_stride_head;  /* elements */
+  void* o; int o_dtype; int64_t o_stride_tok, o_stride_head;        /* elements */
+  const void* k_cache; const void* v_cache;
+  int64_t k_stride_page, k_stride_row, k_stride_head;               /* bytes */
+  int64_t v_stride_page, v_stride_row, v_stride_head;               /* bytes */
+  int64_t num_pages;
+  const int32_t* block_table; int64_t block_table_stride;
+  const int32_t* seq_lens;
+  const int32_t* work; int num_work;
+  const int32_t* n_splits; int max_splits;
+  float* o_part;    /* scratch (max_splits, part_seqs, h_k, n_q, head_size) fp32 */
+  float* lse_part;  /* scratch (max_splits, part_seqs, h_k, n_q) fp32 */
+  int part_seqs;    /* >= num_seqs when any sequence splits */
+  float* lse;       /* optional (num_seqs * q_len, h_q) natural-log LSE */
+  const float* k_descale; int k_descale_mode; /* MJ_SCALE_TENSOR | _HEAD | _SEQ_HEAD */
+  const float* v_descale; int v_descale_mode;
+  const float* q_mul;  /* optional (h_q, head_size): Q *= q_mul (e2m3 K channel scales) */
+  const float* o_mul;  /* optional (h_q, head_size): O *= o_mul (e2m3 V channel scales) */
+  float softmax_scale;
+  int causal;
+  int with_combine;    /* also run mj_combine after the decode */
+  int32_t* status;     /* optional device status word (MJ_DEV_*) */
+} mj_decode_args;
+
+int mj_decode(const mj_decode_args* args, void* stream);
+
+/* LSE merge of the partials of every sequence with n_splits > 1 into O / LSE. */
+int mj_combine(const mj_decode_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MJOLNIR_B200_H */

@@ -1,0 +1,138 @@
+"""ctypes binding of libmjolnir_b200.so (the C ABI in include/mjolnir_b200.h).
+
+The library is built in-tree (``python -m mjolnir_b200.build``). There is no
+fallback: if the library is missing or a call fails, this module raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmjolnir_b200.so")
+
+MJ_OK = 0
+MJ_ERR_INVALID = 1
+MJ_ERR_UNSUPPORTED = 2
+MJ_ERR_CUDA = 3
+MJ_ERR_DEVICE = 4
+
+MJ_DEV_OK = 0
+MJ_DEV_BAD_PAGE = 1
+MJ_DEV_BAD_SPLIT = 2
+MJ_DEV_TIMEOUT = 3
+
+MJ_KV_FP8_E4M3 = 0
+MJ_KV_E2M3 = 1
+KV_FORMATS = {"fp8": MJ_KV_FP8_E4M3, "e2m3": MJ_KV_E2M3}
+
+MJ_DT_BF16 = 0
+MJ_DT_FP16 = 1
+MJ_DT_FP32 = 2
+
+MJ_SCALE_TENSOR = 0
+MJ_SCALE_HEAD = 1
+MJ_SCALE_CHANNEL = 2
+MJ_SCALE_SEQ_HEAD = 3
+
+EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine")
+
+_i64, _i32, _vp, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
+
+
+class CacheWriteArgs(C.Structure):
+    _fields_ = [
+        ("key", _vp), ("value", _vp), ("src_dtype", _i32),
+        ("num_tokens", _i64), ("h_k", _i32), ("head_size", _i32),
+        ("key_stride_tok", _i64), ("key_stride_head", _i64),
+        ("value_stride_tok", _i64), ("value_stride_head", _i64),
+        ("k_cache", _vp), ("v_cache", _vp),
+        ("k_stride_page", _i64), ("k_stride_row", _i64), ("k_stride_head", _i64),
+        ("v_stride_page", _i64), ("v_stride_row", _i64), ("v_stride_head", _i64),
+        ("num_pages", _i64), ("page_size", _i32), ("kv_format", _i32),
+        ("slot_mapping", _vp),
+        ("k_scale", _vp), ("k_scale_mode", _i32),
+        ("v_scale", _vp), ("v_scale_mode", _i32),
+        ("status", _vp),
+    ]
+
+
+class DecodeArgs(C.Structure):
+    _fields_ = [
+        ("num_seqs", _i32), ("q_len", _i32), ("h_q", _i32), ("h_k", _i32),
+        ("head_size", _i32), ("page_size", _i32), ("kv_format", _i32),
+        ("q", _vp), ("q_dtype", _i32), ("q_stride_tok", _i64), ("q_stride_head", _i64),
+        ("o", _vp), ("o_dtype", _i32), ("o_stride_tok", _i64), ("o_stride_head", _i64),
+        ("k_cache", _vp), ("v_cache", _vp),
+        ("k_stride_page", _i64), ("k_stride_row", _i64), ("k_stride_head", _i64),
+        ("v_stride_page", _i64), ("v_stride_row", _i64), ("v_stride_head", _i64),
+        ("num_pages", _i64),
+        ("block_table", _vp), ("block_table_stride", _i64),
+        ("seq_lens", _vp),
+        ("work", _vp), ("num_work", _i32),
+        ("n_splits", _vp), ("max_splits", _i32),
+        ("o_part", _vp), ("lse_part", _vp), ("part_seqs", _i32),
+        ("lse", _vp),
+        ("k_descale", _vp), ("k_descale_mode", _i32),
+        ("v_descale", _vp), ("v_descale_mode", _i32),
+        ("q_mul", _vp), ("o_mul", _vp),
+        ("softmax_scale", _f32), ("causal", _i32), ("with_combine", _i32),
+        ("status", _vp),
+    ]
+
+
+class MjolnirError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"mjolnir_b200 status {code}: {msg}")
+        self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load():
+    """Load the in-tree library (build it first if the sources are newer)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m mjolnir_b200.build` "
+                "(there is no CPU or PyTorch fallback for the hot path)"
+            )
+        lib = C.CDLL(LIB_PATH)
+        lib.mj_last_error.restype = C.c_char_p
+        lib.mj_abi_version.restype = C.c_int
+        lib.mj_row_bytes.argtypes = [C.c_int, C.c_int]
+        lib.mj_row_bytes.restype = C.c_int
+        lib.mj_cache_write.argtypes = [C.POINTER(CacheWriteArgs), _vp]
+        lib.mj_cache_write.restype = C.c_int
+        for fn in ("mj_decode", "mj_combine"):
+            getattr(lib, fn).argtypes = [C.POINTER(DecodeArgs), _vp]
+            getattr(lib, fn).restype = C.c_int
+        _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != MJ_OK:
+        msg = load().mj_last_error().decode(errors="replace")
+        raise MjolnirError(rc, msg)
+
+
+def cache_write(args: CacheWriteArgs, stream: int) -> None:
+    check(load().mj_cache_write(C.byref(args), _vp(stream)))
+
+
+def decode(args: DecodeArgs, stream: int) -> None:
+    check(load().mj_decode(C.byref(args), _vp(stream)))
+
+
+def combine(args: DecodeArgs, stream: int) -> None:
+    check(load().mj_combine(C.byref(args), _vp(stream)))

@@ -1,0 +1,108 @@
+// Device helpers shared by the mjolnir_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mjolnir_b200.h"
+
+namespace mj {
+
+constexpr int kTileRows = 128;  // KV rows per work tile (the planner's unit)
+
+// ---- element loads / stores by runtime dtype ------------------------------
+__device__ __forceinline__ float load_elem(const void* p, int64_t i, int dt) {
+  if (dt == MJ_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == MJ_DT_FP16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_elem(void* p, int64_t i, int dt, float v) {
+  if (dt == MJ_DT_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dt == MJ_DT_FP16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ void flag(int32_t* status, int code) {
+  if (status) atomicExch(status, code);
+}
+
+// ---- e2m3 (sign | 2-bit exp | 3-bit mantissa, bias 1, max 7.5) -----------
+// Value of a magnitude code 0..31, from the bit definition: e == 0 -> m / 8,
+// else (8 + m) * 2^(e - 1) / 8. Exact in fp32 (and in fp16).
+__device__ __forceinline__ float e2m3_mag_value(uint32_t mag) {
+  uint32_t e = mag >> 3, m = mag & 7u;
+  uint32_t eighths = e ? ((8u + m) << (e - 1u)) : m;
+  return (float)eighths * 0.125f;
+}
+
+__device__ __forceinline__ float e2m3_value(uint32_t code) {
+  float v = e2m3_mag_value(code & 31u);
+  return (code & 32u) ? -v : v;
+}
+
+// fp32 (already divided by the scale) -> e2m3 code 0..63: round to nearest,
+// ties to the smaller magnitude, saturating at 7.5 (NaN -> 7.5), the sign bit
+// only for a non-zero magnitude. The neighbour comparison is the reference's
+// fp32 expression (ax - lo) <= (hi - ax) (quant.py:43), evaluated with
+// explicitly rounded subtractions.
+__device__ __forceinline__ uint32_t e2m3_code(float x) {
+  float ax = fabsf(x);
+  uint32_t mag;
+  if (!(ax < 7.5f)) {  // >= 7.5, +-inf or NaN
+    mag = 31u;
+  } else {
+    uint32_t lo;
+    float lo_v, step;
+    if (ax < 2.0f) {           // codes 0..16, spacing 1/8
+      lo = (uint32_t)(ax * 8.0f);
+      lo_v = (float)lo * 0.125f;
+      step = 0.125f;
+    } else if (ax < 4.0f) {    // codes 16..24, spacing 1/4
+      uint32_t k = (uint32_t)((ax - 2.0f) * 4.0f);
+      lo = 16u + k;
+      lo_v = 2.0f + (float)k * 0.25f;
+      step = 0.25f;
+    } else {                   // codes 24..31, spacing 1/2
+      uint32_t k = (uint32_t)((ax - 4.0f) * 2.0f);
+      lo = 24u + k;
+      lo_v = 4.0f + (float)k * 0.5f;
+      step = 0.5f;
+    }
+    if (ax == lo_v) {
+      mag = lo;
+    } else {
+      float hi_v = lo_v + step;
+      bool pick_lo = __fsub_rn(ax, lo_v) <= __fsub_rn(hi_v, ax);
+      mag = pick_lo ? lo : lo + 1u;
+    }
+  }
+  uint32_t neg = (x < 0.0f && mag != 0u) ? 32u : 0u;
+  return mag | neg;
+}
+
+// fp32 -> e4m3fn byte: round to nearest even, saturate at +-448, NaN keeps
+// its sign bit (0x7F / 0xFF).
+__device__ __forceinline__ uint8_t e4m3_byte(float x) {
+  if (isnan(x)) return (uint8_t)(0x7Fu | (signbit(x) ? 0x80u : 0u));
+  x = fminf(fmaxf(x, -448.0f), 448.0f);
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ float e4m3_value(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Descale of (seq, head) under a mode.
+__device__ __forceinline__ float descale_at(const float* p, int mode, int seq, int h, int h_k) {
+  if (!p) return 1.0f;
+  if (mode == MJ_SCALE_TENSOR) return p[0];
+  if (mode == MJ_SCALE_HEAD) return p[h];
+  return p[(int64_t)seq * h_k + h];
+}
+
+}  // namespace mj

@@ -1,0 +1,152 @@
+"""Decode parity on the B200: the CUDA path through the C ABI vs the CPU oracle
+(pinned to the reference) and vs the reference's own outputs (golden)."""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention, quant
+from tests.conftest import GOLDEN
+from tests.helpers import Case, assert_close_bf16, assert_close_fp32
+
+pytestmark = pytest.mark.gpu
+
+
+def test_golden_reference_outputs():
+    """The kernel on the reference's own fixtures vs the reference's ref_decode output."""
+    from mjolnir_b200.runner import DecodeRunner
+
+    g = np.load(os.path.join(GOLDEN, "decode.npz"))
+    names = sorted({k.split("__")[0] for k in g.files})
+    for name in names:
+        ql, h_q, h_k, d, PS, causal, e2m3 = (int(v) for v in g[name + "__meta"])
+        fmt = "e2m3" if e2m3 else "fp8"
+        kb = torch.from_numpy(g[name + "__k_bytes"]).cuda()
+        vb = torch.from_numpy(g[name + "__v_bytes"]).cuda()
+        sl = torch.from_numpy(g[name + "__seq_lens"]).to(torch.int32)
+        bt = torch.from_numpy(g[name + "__block_table"]).to(torch.int32)
+        b = len(sl)
+        q = torch.from_numpy(g[name + "__q_bits"]).view(torch.bfloat16).cuda()
+        kd = torch.from_numpy(g[name + "__k_descale"]).cuda()
+        vd = torch.from_numpy(g[name + "__v_descale"]).cuda()
+        for sm in (148, 2):  # 148 SMs: small batches split; 2 SMs: whole sequences
+            r = DecodeRunner(num_heads=h_q, num_kv_heads=h_k, head_size=d, page_size=PS, max_num_seqs=b,
+                             max_q_len=ql, kv_format=fmt, sm_count=sm)
+            plan = r.plan(sl.tolist(), b, ql, bt.cuda(), sl.cuda(), causal=bool(causal))
+            out = torch.full((b * ql, h_q, d), float("nan"), dtype=torch.float32, device="cuda")
+            r.run(plan, q, out, kb, vb, kd, vd, 1.0 / math.sqrt(d))
+            torch.cuda.synchronize()
+            r.check_status()
+            ref = torch.from_numpy(g[name + "__o_ref"])
+            assert_close_fp32(out, ref, what=f"{name} sm={sm} splits={plan.with_reduction}")
+
+
+@pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
+@pytest.mark.parametrize("layout", ["BHN2D", "BNH2D", "B2NHD", "B2HND", "2BNHD", "2BHND"])
+def test_layouts(kv_format, layout):
+    c = Case(seq_lens=(300, 1, 2049, 128), h_q=16, h_k=2, kv_format=kv_format, layout=layout, seed=3)
+    out, _, _ = c.run()
+    ref, _ = c.oracle()
+    T = c.b * c.q_len
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"{kv_format}/{layout}")
+    assert torch.isnan(out[T:]).all(), "wrote past the batch"
+
+
+def test_config1_shape():
+    """b 4, 8 q / 2 KV heads, d 128, PS 16, L ~ U[1, 2048], fp8 scale 1.0."""
+    g = torch.Generator().manual_seed(1)
+    lens = torch.randint(1, 2049, (4,), generator=g).tolist()
+    c = Case(seq_lens=lens, h_q=8, h_k=2, kv_format="fp8", layout="B2NHD", seed=1)
+    for out_dtype in (torch.float32, torch.bfloat16):
+        out, lse, plan = c.run(out_dtype=out_dtype, lse=True)
+        ref, ref_lse = c.oracle()
+        T = c.b
+        got = out[:T].view(T, c.h_q, c.d)
+        if out_dtype == torch.float32:
+            assert_close_fp32(got, ref, what="config1 fp32")
+            assert torch.allclose(lse.cpu(), ref_lse, atol=1e-4, rtol=1e-5)
+        else:
+            assert_close_bf16(got, ref, what="config1 bf16")
+
+
+@pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
+@pytest.mark.parametrize("q_len,causal", [(4, True), (6, True), (3, False)])
+def test_mtp_rows(kv_format, q_len, causal):
+    c = Case(seq_lens=(q_len, 700, 1500, 33), q_len=q_len, h_q=16, h_k=2, kv_format=kv_format, seed=5,
+             descale="head" if kv_format == "fp8" else "tensor")
+    out, _, _ = c.run(causal=causal)
+    ref, _ = c.oracle()
+    T = c.b * q_len
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"mtp q_len {q_len}")
+
+
+@pytest.mark.parametrize("sm_count", [148, 4])
+def test_split_and_unsplit_agree(sm_count):
+    """Small sm_count: no split; 148 SMs with 3 sequences: every sequence splits."""
+    c = Case(seq_lens=(5000, 3000, 129), h_q=32, h_k=8, kv_format="e2m3", seed=7, outliers=0.01)
+    out, _, plan = c.run(sm_count=sm_count)
+    assert plan.with_reduction == (sm_count == 148)
+    ref, _ = c.oracle()
+    T = c.b
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"sm {sm_count}")
+
+
+def test_descale_per_seq_head_and_d256():
+    c = Case(seq_lens=(77, 150, 1000), q_len=2, h_q=8, h_k=1, d=256, page_size=64, kv_format="fp8",
+             layout="BHN2D", descale="seqhead", seed=9)
+    out, _, _ = c.run()
+    ref, _ = c.oracle()
+    T = c.b * 2
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what="d256 seqhead")
+
+
+def test_empty_rows_and_fixed_grid():
+    """L < q_len leaves the first draft rows with no visible key: O = 0. A
+    padded fixed grid (CUDA-graph mode) gives the same result."""
+    c = Case(seq_lens=(2, 400), q_len=4, h_q=8, h_k=2, kv_format="fp8", seed=11)
+    out, _, _ = c.run(fixed_grid=True)
+    ref, _ = c.oracle()
+    T = c.b * 4
+    got = out[:T].view(T, c.h_q, c.d)
+    assert (got[:2] == 0).all()
+    assert_close_fp32(got, ref, what="empty rows")
+
+
+def test_graph_replay_with_new_plan():
+    """Capture once with a fixed grid, re-plan (different lengths), replay."""
+    c = Case(seq_lens=(900, 40, 2100), h_q=16, h_k=2, kv_format="fp8", seed=13, max_num_seqs=4)
+    r = c.runner()
+    T = c.b
+    out = torch.zeros(T, c.h_q * c.d, dtype=torch.float32, device="cuda")
+    kd, vd = c.dev(c.kd), c.dev(c.vd)
+    plan = r.plan(c.seq_lens, c.b, 1, c.block_table, c.seq_lens_t, fixed_grid=True)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        r.run(plan, c.query, out, c.k_view, c.v_view, kd, vd, 1.0 / math.sqrt(c.d))
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        r.run(plan, c.query, out, c.k_view, c.v_view, kd, vd, 1.0 / math.sqrt(c.d))
+    new_lens = [700, 40, 1900]
+    c.seq_lens_t[: c.b].copy_(torch.tensor(new_lens, dtype=torch.int32))
+    r.plan(new_lens, c.b, 1, c.block_table, c.seq_lens_t, fixed_grid=True)
+    graph.replay()
+    torch.cuda.synchronize()
+    c.seq_lens = new_lens
+    ref, _ = c.oracle()
+    assert_close_fp32(out.view(T, c.h_q, c.d), ref, what="graph replay")
+
+
+def test_bad_page_sets_status_not_fault():
+    """A block-table entry past the pool is flagged in the status word and
+    skipped (no out-of-bounds read)."""
+    from mjolnir_b200 import _lib
+
+    c = Case(seq_lens=(100,), h_q=8, h_k=2, kv_format="fp8", seed=17)
+    c.block_table[0, 1] = c.num_pages + 5  # in bounds of the table, out of the pool
+    with pytest.raises(_lib.MjolnirError):
+        c.run()
