@@ -51,11 +51,12 @@ __global__ void __launch_bounds__(256) cache_write_kernel(mj_cache_write_args a)
                    row * (side ? a.v_stride_row : a.k_stride_row) +
                    h * (side ? a.v_stride_head : a.k_stride_head);
     for (int g = lane; g < groups; g += 32) {
-      float x[4];
+      float x[4], xin[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int c = 4 * g + i;
-        x[i] = __fdiv_rn(load_elem(src, base + c, a.src_dtype), scale_of(sc, mode, h, c, d));
+        xin[i] = load_elem(src, base + c, a.src_dtype);
+        x[i] = __fdiv_rn(xin[i], scale_of(sc, mode, h, c, d));
       }
       if (FMT == MJ_KV_E2M3) {
         uint32_t w = e2m3_code(x[0]) | (e2m3_code(x[1]) << 6) | (e2m3_code(x[2]) << 12) |
@@ -64,8 +65,11 @@ __global__ void __launch_bounds__(256) cache_write_kernel(mj_cache_write_args a)
         dst[3 * g + 1] = (uint8_t)((w >> 8) & 0xFFu);
         dst[3 * g + 2] = (uint8_t)((w >> 16) & 0xFFu);
       } else {
+        // A NaN input keeps its sign bit (0x7F / 0xFF) as the reference's host
+        // division does; the device division returns a canonical NaN.
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[4 * g + i] = e4m3_byte(x[i]);
+        for (int i = 0; i < 4; ++i)
+          dst[4 * g + i] = isnan(x[i]) ? (uint8_t)(0x7Fu | (signbit(xin[i]) ? 0x80u : 0u)) : e4m3_byte(x[i]);
       }
     }
   }

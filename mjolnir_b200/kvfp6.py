@@ -33,20 +33,20 @@ def row_bytes(head_size: int) -> int:
     return _row_bytes(head_size, "e2m3")
 
 
-def reshape_and_cache(
-    key: torch.Tensor,  # (>= T, h_k, d) bf16/fp16/fp32, d contiguous
+def cache_write_args(
+    key: torch.Tensor,
     value: torch.Tensor,
-    k_cache: torch.Tensor,  # logical (pages, page_size, h_k, row) uint8 / float8 view
+    k_cache: torch.Tensor,
     v_cache: torch.Tensor,
-    slot_mapping: torch.Tensor,  # (T,) int64 (int32 accepted), -1 = padding
-    k_scale: torch.Tensor,  # fp32: 1 elem, (h_k,) or (h_k, d)
+    slot_mapping: torch.Tensor,
+    k_scale: torch.Tensor,
     v_scale: torch.Tensor,
     kv_format: str,
     status: torch.Tensor | None = None,
-) -> None:
+) -> _lib.CacheWriteArgs:
+    """Validated ``mj_cache_write`` arguments for these tensors (they must
+    stay alive while the returned struct is used)."""
     T = slot_mapping.shape[0]
-    if T == 0:
-        return
     _, h_k, d = key.shape
     if key.stride(2) != 1 or value.stride(2) != 1:
         raise ValueError("key / value head dim must be contiguous")
@@ -59,9 +59,9 @@ def reshape_and_cache(
         if t.element_size() != 1:
             raise TypeError("cache views must be byte views (uint8 / float8)")
     if slot_mapping.dtype != torch.int64:
-        slot_mapping = slot_mapping.to(torch.int64)
-    k_scale = k_scale.to(torch.float32).contiguous()
-    v_scale = v_scale.to(torch.float32).contiguous()
+        raise TypeError("slot_mapping must be int64")
+    if k_scale.dtype != torch.float32 or v_scale.dtype != torch.float32:
+        raise TypeError("KV scales must be fp32")
     a = _lib.CacheWriteArgs()
     a.key, a.value, a.src_dtype = key.data_ptr(), value.data_ptr(), dtype_code(key.dtype)
     if value.dtype != key.dtype:
@@ -78,6 +78,28 @@ def reshape_and_cache(
     a.k_scale, a.k_scale_mode = k_scale.data_ptr(), scale_mode(k_scale, h_k, d)
     a.v_scale, a.v_scale_mode = v_scale.data_ptr(), scale_mode(v_scale, h_k, d)
     a.status = None if status is None else status.data_ptr()
+    return a
+
+
+def reshape_and_cache(
+    key: torch.Tensor,  # (>= T, h_k, d) bf16/fp16/fp32, d contiguous
+    value: torch.Tensor,
+    k_cache: torch.Tensor,  # logical (pages, page_size, h_k, row) uint8 / float8 view
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,  # (T,) int64 (int32 accepted), -1 = padding
+    k_scale: torch.Tensor,  # fp32: 1 elem, (h_k,) or (h_k, d)
+    v_scale: torch.Tensor,
+    kv_format: str,
+    status: torch.Tensor | None = None,
+) -> None:
+    """Quantize, pack and scatter T new K/V rows into the cache views."""
+    if slot_mapping.shape[0] == 0:
+        return
+    if slot_mapping.dtype != torch.int64:
+        slot_mapping = slot_mapping.to(torch.int64)
+    k_scale = k_scale.to(torch.float32).contiguous()
+    v_scale = v_scale.to(torch.float32).contiguous()
+    a = cache_write_args(key, value, k_cache, v_cache, slot_mapping, k_scale, v_scale, kv_format, status)
     _lib.cache_write(a, _stream(key.device))
 
 
