@@ -228,14 +228,20 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(workload, kv):
-    """dram bytes per decode launch from a committed ncu summary, if present."""
+def profiled_traffic(kernel, workload, kv, algorithmic):
+    """DRAM bytes per decode launch from the committed ncu capture of this
+    kernel: the measured bytes when the capture was this workload, else the
+    capture's traffic / algorithmic ratio scaled to this launch's bytes."""
     p = os.path.join(ROOT, "profiles", "decode_traffic.json")
     if not os.path.exists(p):
         return None
     with open(p) as f:
-        j = json.load(f)
-    return j.get(f"{workload}-{kv}")
+        j = json.load(f).get(kernel)
+    if not j:
+        return None
+    if j["captured_on"] == f"{workload}-{kv}":
+        return int(j["dram_bytes_per_launch"])
+    return int(round(j["traffic_over_algorithmic"] * algorithmic))
 
 
 # ---------------------------------------------------------------------------
@@ -434,7 +440,7 @@ def main():
     peak, peak_kind = peaks()
     alg = wl.algorithmic_decode_bytes()
     achieved = alg / (dec_ms_max * 1e-3) / 1e9
-    traffic = profiled_traffic(args.workload, wl.fmt)
+    traffic = profiled_traffic(wl.runner.kernel_name(wl.plan), args.workload, wl.fmt, alg)
     line = {
         "metric": "decode-attn KV GB/s",
         "value": round(total_kv / (ms * 1e-3) / 1e9, 2),

@@ -381,6 +381,10 @@ class DecodeRunner:
         _lib.decode(a, _stream(self.device))
         return out
 
+    def kernel_name(self, plan: StepPlan) -> str:
+        """The decode kernel this runner launches for a plan."""
+        return "decode_simt"
+
     def check_status(self) -> None:
         """Raise if a kernel flagged a bad page / split index (synchronizes)."""
         code = int(self.status.item())
