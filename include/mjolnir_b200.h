@@ -159,6 +159,22 @@ int mj_decode(const mj_decode_args* args, void* stream);
 /* LSE merge of the partials of every sequence with n_splits > 1 into O / LSE. */
 int mj_combine(const mj_decode_args* args, void* stream);
 
+/* mj_decode for callers that cannot allocate device memory. No counterpart
+ * in the reference. Engines that pre-size all of HBM into their own pools,
+ * code issuing work during a global-mode stream capture (where cudaMalloc is
+ * illegal) and plugin hosts that pass only inputs and outputs cannot supply
+ * o_part / lse_part; this entry point ignores those fields (and part_seqs)
+ * and keeps the partials in a 16 MiB device array built into the library,
+ * which every GPU that loads the library holds until exit. It allocates
+ * nothing. The merge always runs inside the call (with_combine is forced on).
+ * Limit: max_splits * num_seqs * h_k * (q_len * h_q / h_k) * (head_size + 1)
+ * * 4 bytes <= 16 MiB, else MJ_ERR_UNSUPPORTED with a message. The first call
+ * on each device looks the array up (cudaGetSymbolAddress) -- make it before
+ * any stream capture. All calls on a device share the array and it keeps the
+ * last call's contents (nothing in it needs to start at zero); calls that
+ * overlap on the GPU race on it and must be ordered. */
+int mj_decode_noalloc(const mj_decode_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

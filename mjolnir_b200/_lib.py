@@ -37,7 +37,8 @@ MJ_SCALE_HEAD = 1
 MJ_SCALE_CHANNEL = 2
 MJ_SCALE_SEQ_HEAD = 3
 
-EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine")
+EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine",
+            "mj_decode_noalloc")
 
 _i64, _i32, _vp, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
 
@@ -113,7 +114,7 @@ def load():
         lib.mj_row_bytes.restype = C.c_int
         lib.mj_cache_write.argtypes = [C.POINTER(CacheWriteArgs), _vp]
         lib.mj_cache_write.restype = C.c_int
-        for fn in ("mj_decode", "mj_combine"):
+        for fn in ("mj_decode", "mj_combine", "mj_decode_noalloc"):
             getattr(lib, fn).argtypes = [C.POINTER(DecodeArgs), _vp]
             getattr(lib, fn).restype = C.c_int
         _lib = lib
@@ -136,3 +137,9 @@ def decode(args: DecodeArgs, stream: int) -> None:
 
 def combine(args: DecodeArgs, stream: int) -> None:
     check(load().mj_combine(C.byref(args), _vp(stream)))
+
+
+def decode_noalloc(args: DecodeArgs, stream: int) -> None:
+    """mj_decode with the split-KV partials kept in the library's built-in
+    16 MiB device array, for callers that cannot allocate device memory."""
+    check(load().mj_decode_noalloc(C.byref(args), _vp(stream)))

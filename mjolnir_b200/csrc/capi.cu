@@ -32,6 +32,11 @@ static int cuda_status(cudaError_t e, const char* what) {
 
 static bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p % a) == 0; }
 
+namespace mj {
+// Lets other translation units of the library report through mj_last_error().
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace mj
+
 extern "C" {
 
 const char* mj_last_error(void) { return g_err; }
