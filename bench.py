@@ -440,7 +440,8 @@ def main():
     peak, peak_kind = peaks()
     alg = wl.algorithmic_decode_bytes()
     achieved = alg / (dec_ms_max * 1e-3) / 1e9
-    traffic = profiled_traffic(wl.runner.kernel_name(wl.plan), args.workload, wl.fmt, alg)
+    kname = wl.runner.kernel_name(da)
+    traffic = profiled_traffic(kname, args.workload, wl.fmt, alg)
     line = {
         "metric": "decode-attn KV GB/s",
         "value": round(total_kv / (ms * 1e-3) / 1e9, 2),
@@ -461,7 +462,7 @@ def main():
                    "work_items": wl.plan.num_chunks},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "mj_decode", "peak_source": peak_kind,
+                     "kernel": kname, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": alg, "launch_ms": round(dec_ms_max, 4)},
         "cpu_baseline": cpu,
         "e2e": {"value": round(total_kv / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),

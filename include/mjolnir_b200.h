@@ -68,6 +68,13 @@ extern "C" {
 #define MJ_DT_FP16 1
 #define MJ_DT_FP32 2
 
+/* decode kernels: AUTO picks the tensor-core kernel when it can run the
+ * arguments (head_size 128, <= 16 query rows per KV head, page 16..128,
+ * TMA-aligned KV views), else the CUDA-core kernel; TC demands the former. */
+#define MJ_KERNEL_AUTO 0
+#define MJ_KERNEL_SIMT 1
+#define MJ_KERNEL_TC 2
+
 /* scale / descale modes */
 #define MJ_SCALE_TENSOR 0   /* one fp32 */
 #define MJ_SCALE_HEAD 1     /* (h_k,) fp32 */
@@ -151,10 +158,15 @@ typedef struct mj_decode_args {
   float softmax_scale;
   int causal;
   int with_combine;    /* also run mj_combine after the decode */
+  int kernel;          /* MJ_KERNEL_AUTO, MJ_KERNEL_SIMT or MJ_KERNEL_TC */
   int32_t* status;     /* optional device status word (MJ_DEV_*) */
 } mj_decode_args;
 
 int mj_decode(const mj_decode_args* args, void* stream);
+
+/* The kernel mj_decode would launch for these arguments: MJ_KERNEL_SIMT or
+ * MJ_KERNEL_TC (a negative status if the arguments are invalid). */
+int mj_decode_kernel(const mj_decode_args* args);
 
 /* LSE merge of the partials of every sequence with n_splits > 1 into O / LSE. */
 int mj_combine(const mj_decode_args* args, void* stream);

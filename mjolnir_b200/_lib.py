@@ -32,13 +32,18 @@ MJ_DT_BF16 = 0
 MJ_DT_FP16 = 1
 MJ_DT_FP32 = 2
 
+MJ_KERNEL_AUTO = 0
+MJ_KERNEL_SIMT = 1
+MJ_KERNEL_TC = 2
+KERNEL_NAMES = {MJ_KERNEL_SIMT: "decode_simt", MJ_KERNEL_TC: "decode_tc"}
+
 MJ_SCALE_TENSOR = 0
 MJ_SCALE_HEAD = 1
 MJ_SCALE_CHANNEL = 2
 MJ_SCALE_SEQ_HEAD = 3
 
 EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine",
-            "mj_decode_noalloc")
+            "mj_decode_noalloc", "mj_decode_kernel")
 
 _i64, _i32, _vp, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
 
@@ -80,6 +85,7 @@ class DecodeArgs(C.Structure):
         ("v_descale", _vp), ("v_descale_mode", _i32),
         ("q_mul", _vp), ("o_mul", _vp),
         ("softmax_scale", _f32), ("causal", _i32), ("with_combine", _i32),
+        ("kernel", _i32),
         ("status", _vp),
     ]
 
@@ -117,6 +123,8 @@ def load():
         for fn in ("mj_decode", "mj_combine", "mj_decode_noalloc"):
             getattr(lib, fn).argtypes = [C.POINTER(DecodeArgs), _vp]
             getattr(lib, fn).restype = C.c_int
+        lib.mj_decode_kernel.argtypes = [C.POINTER(DecodeArgs)]
+        lib.mj_decode_kernel.restype = C.c_int
         _lib = lib
     return _lib
 
@@ -133,6 +141,14 @@ def cache_write(args: CacheWriteArgs, stream: int) -> None:
 
 def decode(args: DecodeArgs, stream: int) -> None:
     check(load().mj_decode(C.byref(args), _vp(stream)))
+
+
+def decode_kernel(args: DecodeArgs) -> int:
+    """MJ_KERNEL_SIMT or MJ_KERNEL_TC: the kernel mj_decode would launch."""
+    rc = load().mj_decode_kernel(C.byref(args))
+    if rc < 0:
+        check(-rc)
+    return rc
 
 
 def combine(args: DecodeArgs, stream: int) -> None:

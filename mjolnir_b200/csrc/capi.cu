@@ -10,6 +10,8 @@ namespace mj {
 cudaError_t launch_cache_write(const mj_cache_write_args& a, cudaStream_t stream);
 cudaError_t launch_decode_simt(const mj_decode_args& a, cudaStream_t stream);
 cudaError_t launch_combine(const mj_decode_args& a, cudaStream_t stream);
+cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool* handled);
+const char* tc_ineligible(const mj_decode_args& a);
 }  // namespace mj
 
 static thread_local char g_err[512] = "";
@@ -97,7 +99,18 @@ static int validate_decode(const mj_decode_args& a, const char* who) {
       return fail(MJ_ERR_INVALID, "%s: descale mode %d", who, m);
   if (a.o_part && (!a.lse_part || a.part_seqs < a.num_seqs))
     return fail(MJ_ERR_INVALID, "%s: partial buffers need lse_part and part_seqs >= num_seqs", who);
+  if (a.kernel < MJ_KERNEL_AUTO || a.kernel > MJ_KERNEL_TC) return fail(MJ_ERR_INVALID, "%s: kernel %d", who, a.kernel);
+  if (a.kernel == MJ_KERNEL_TC && mj::tc_ineligible(a))
+    return fail(MJ_ERR_UNSUPPORTED, "%s: the tensor-core kernel cannot run these arguments (%s)", who, mj::tc_ineligible(a));
   return MJ_OK;
+}
+
+int mj_decode_kernel(const mj_decode_args* args) {
+  if (!args) return -fail(MJ_ERR_INVALID, "mj_decode_kernel: null args");
+  int rc = validate_decode(*args, "mj_decode_kernel");
+  if (rc) return -rc;
+  if (args->kernel == MJ_KERNEL_SIMT) return MJ_KERNEL_SIMT;
+  return mj::tc_ineligible(*args) ? MJ_KERNEL_SIMT : MJ_KERNEL_TC;
 }
 
 int mj_decode(const mj_decode_args* args, void* stream) {
@@ -110,8 +123,16 @@ int mj_decode(const mj_decode_args* args, void* stream) {
     return MJ_OK;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t e = mj::launch_decode_simt(a, s);
-  if (e != cudaSuccess) return cuda_status(e, "mj_decode launch");
+  bool handled = false;
+  cudaError_t e = cudaSuccess;
+  if (a.kernel != MJ_KERNEL_SIMT) {
+    e = mj::launch_decode_tc(a, s, &handled);
+    if (e != cudaSuccess) return cuda_status(e, "mj_decode launch (tensor-core kernel)");
+  }
+  if (!handled) {
+    e = mj::launch_decode_simt(a, s);
+    if (e != cudaSuccess) return cuda_status(e, "mj_decode launch");
+  }
   if (a.with_combine) {
     if (!a.o_part) return fail(MJ_ERR_INVALID, "mj_decode: with_combine needs partial buffers");
     return cuda_status(mj::launch_combine(a, s), "mj_combine launch");

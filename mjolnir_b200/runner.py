@@ -169,6 +169,9 @@ def descale_mode(t: torch.Tensor, num_seqs: int, h_k: int) -> int:
     raise ValueError(f"descale shape {tuple(t.shape)} (1, (h_k,) or contiguous (b, h_k))")
 
 
+_KERNELS = {"auto": _lib.MJ_KERNEL_AUTO, "simt": _lib.MJ_KERNEL_SIMT, "tc": _lib.MJ_KERNEL_TC}
+
+
 def _ptr(t):
     return None if t is None else t.data_ptr()
 
@@ -204,6 +207,7 @@ class DecodeRunner:
         device: torch.device | str = "cuda",
         sm_count: int | None = None,
         rebalance: bool = True,
+        kernel: str | None = None,
     ):
         if num_heads % num_kv_heads:
             raise ValueError("num_heads must be a multiple of num_kv_heads")
@@ -226,6 +230,11 @@ class DecodeRunner:
         self.kv_format = kv_format
         self.kv_row_bytes = row_bytes(head_size, kv_format)
         self.rebalance = rebalance
+        # decode kernel: "auto" (tensor-core kernel where it applies), "simt" or "tc"
+        kernel = (kernel or env_flag("MJOLNIR_ATTN_KERNEL", "auto")).lower()
+        if kernel not in _KERNELS:
+            raise ValueError(f"kernel must be one of {tuple(_KERNELS)}")
+        self.kernel = _KERNELS[kernel]
         self.device = torch.device(device)
         if sm_count is None:
             sm_count = torch.cuda.get_device_properties(self.device).multi_processor_count
@@ -360,6 +369,7 @@ class DecodeRunner:
         a.softmax_scale = float(softmax_scale)
         a.causal = int(plan.causal)
         a.with_combine = int(plan.with_reduction)
+        a.kernel = self.kernel
         a.status = self.status.data_ptr()
         return a
 
@@ -381,9 +391,9 @@ class DecodeRunner:
         _lib.decode(a, _stream(self.device))
         return out
 
-    def kernel_name(self, plan: StepPlan) -> str:
-        """The decode kernel this runner launches for a plan."""
-        return "decode_simt"
+    def kernel_name(self, args: _lib.DecodeArgs) -> str:
+        """The decode kernel mj_decode launches for these arguments."""
+        return _lib.KERNEL_NAMES[_lib.decode_kernel(args)]
 
     def check_status(self) -> None:
         """Raise if a kernel flagged a bad page / split index (synchronizes)."""

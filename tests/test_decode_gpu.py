@@ -32,36 +32,54 @@ def test_golden_reference_outputs():
         q = torch.from_numpy(g[name + "__q_bits"]).view(torch.bfloat16).cuda()
         kd = torch.from_numpy(g[name + "__k_descale"]).cuda()
         vd = torch.from_numpy(g[name + "__v_descale"]).cuda()
-        for sm in (148, 2):  # 148 SMs: small batches split; 2 SMs: whole sequences
+        kernels = ["simt"] + (["tc"] if d == 128 and ql * h_q // h_k <= 16 else [])
+        for sm, kernel in [(sm, k) for sm in (148, 2) for k in kernels]:  # 148 SMs: small batches split
             r = DecodeRunner(num_heads=h_q, num_kv_heads=h_k, head_size=d, page_size=PS, max_num_seqs=b,
-                             max_q_len=ql, kv_format=fmt, sm_count=sm)
+                             max_q_len=ql, kv_format=fmt, sm_count=sm, kernel=kernel)
             plan = r.plan(sl.tolist(), b, ql, bt.cuda(), sl.cuda(), causal=bool(causal))
             out = torch.full((b * ql, h_q, d), float("nan"), dtype=torch.float32, device="cuda")
             r.run(plan, q, out, kb, vb, kd, vd, 1.0 / math.sqrt(d))
             torch.cuda.synchronize()
             r.check_status()
             ref = torch.from_numpy(g[name + "__o_ref"])
-            assert_close_fp32(out, ref, what=f"{name} sm={sm} splits={plan.with_reduction}")
+            assert_close_fp32(out, ref, what=f"{name} {kernel} sm={sm} splits={plan.with_reduction}")
+
+
+def _kernel_of(c, **kw):
+    from mjolnir_b200 import _lib
+
+    r = c.runner(**kw)
+    plan = r.plan(c.seq_lens, c.b, c.q_len, c.block_table, c.seq_lens_t)
+    out = torch.empty(c.b * c.q_len, c.h_q * c.d, device="cuda")
+    args = r.decode_args(plan, c.query, out, c.k_view, c.v_view, c.dev(c.kd), c.dev(c.vd), 0.1,
+                         q_mul=c.dev(c.q_mul), o_mul=c.dev(c.o_mul))
+    return _lib.KERNEL_NAMES[_lib.decode_kernel(args)]
 
 
 @pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
 @pytest.mark.parametrize("layout", ["BHN2D", "BNH2D", "B2NHD", "B2HND", "2BNHD", "2BHND"])
-def test_layouts(kv_format, layout):
+@pytest.mark.parametrize("kernel", ["simt", "auto"])
+def test_layouts(kv_format, layout, kernel):
     c = Case(seq_lens=(300, 1, 2049, 128), h_q=16, h_k=2, kv_format=kv_format, layout=layout, seed=3)
-    out, _, _ = c.run()
+    # every vLLM layout gives TMA-legal strides here (e2m3 rows are 96 B, a
+    # multiple of the 32 B the 16U6 type needs)
+    expect = "decode_simt" if kernel == "simt" else "decode_tc"
+    assert _kernel_of(c, kernel=kernel) == expect
+    out, _, _ = c.run(kernel=kernel)
     ref, _ = c.oracle()
     T = c.b * c.q_len
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"{kv_format}/{layout}")
     assert torch.isnan(out[T:]).all(), "wrote past the batch"
 
 
-def test_config1_shape():
+@pytest.mark.parametrize("kernel", ["simt", "tc"])
+def test_config1_shape(kernel):
     """b 4, 8 q / 2 KV heads, d 128, PS 16, L ~ U[1, 2048], fp8 scale 1.0."""
     g = torch.Generator().manual_seed(1)
     lens = torch.randint(1, 2049, (4,), generator=g).tolist()
     c = Case(seq_lens=lens, h_q=8, h_k=2, kv_format="fp8", layout="B2NHD", seed=1)
     for out_dtype in (torch.float32, torch.bfloat16):
-        out, lse, plan = c.run(out_dtype=out_dtype, lse=True)
+        out, lse, plan = c.run(out_dtype=out_dtype, lse=True, kernel=kernel)
         ref, ref_lse = c.oracle()
         T = c.b
         got = out[:T].view(T, c.h_q, c.d)
@@ -73,21 +91,23 @@ def test_config1_shape():
 
 
 @pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
-@pytest.mark.parametrize("q_len,causal", [(4, True), (6, True), (3, False)])
-def test_mtp_rows(kv_format, q_len, causal):
-    c = Case(seq_lens=(q_len, 700, 1500, 33), q_len=q_len, h_q=16, h_k=2, kv_format=kv_format, seed=5,
-             descale="head" if kv_format == "fp8" else "tensor")
-    out, _, _ = c.run(causal=causal)
+@pytest.mark.parametrize("q_len,causal,h_q,kernel", [(4, True, 16, "simt"), (6, True, 16, "simt"), (3, False, 16, "simt"),
+                                                     (4, True, 8, "tc"), (2, False, 16, "tc"), (3, True, 8, "tc")])
+def test_mtp_rows(kv_format, q_len, causal, h_q, kernel):
+    c = Case(seq_lens=(q_len, 700, 1500, 33), q_len=q_len, h_q=h_q, h_k=2, kv_format=kv_format, seed=5,
+             descale="head" if kv_format == "fp8" else "tensor", layout="BHN2D")
+    out, _, _ = c.run(causal=causal, kernel=kernel)
     ref, _ = c.oracle()
     T = c.b * q_len
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"mtp q_len {q_len}")
 
 
 @pytest.mark.parametrize("sm_count", [148, 4])
-def test_split_and_unsplit_agree(sm_count):
+@pytest.mark.parametrize("kernel", ["simt", "tc"])
+def test_split_and_unsplit_agree(sm_count, kernel):
     """Small sm_count: no split; 148 SMs with 3 sequences: every sequence splits."""
-    c = Case(seq_lens=(5000, 3000, 129), h_q=32, h_k=8, kv_format="e2m3", seed=7, outliers=0.01)
-    out, _, plan = c.run(sm_count=sm_count)
+    c = Case(seq_lens=(5000, 3000, 129), h_q=32, h_k=8, kv_format="e2m3", seed=7, outliers=0.01, layout="BHN2D")
+    out, _, plan = c.run(sm_count=sm_count, kernel=kernel)
     assert plan.with_reduction == (sm_count == 148)
     ref, _ = c.oracle()
     T = c.b
@@ -103,11 +123,12 @@ def test_descale_per_seq_head_and_d256():
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what="d256 seqhead")
 
 
-def test_empty_rows_and_fixed_grid():
+@pytest.mark.parametrize("kernel", ["simt", "tc"])
+def test_empty_rows_and_fixed_grid(kernel):
     """L < q_len leaves the first draft rows with no visible key: O = 0. A
     padded fixed grid (CUDA-graph mode) gives the same result."""
     c = Case(seq_lens=(2, 400), q_len=4, h_q=8, h_k=2, kv_format="fp8", seed=11)
-    out, _, _ = c.run(fixed_grid=True)
+    out, _, _ = c.run(fixed_grid=True, kernel=kernel)
     ref, _ = c.oracle()
     T = c.b * 4
     got = out[:T].view(T, c.h_q, c.d)
@@ -115,10 +136,11 @@ def test_empty_rows_and_fixed_grid():
     assert_close_fp32(got, ref, what="empty rows")
 
 
-def test_graph_replay_with_new_plan():
+@pytest.mark.parametrize("kernel", ["simt", "tc"])
+def test_graph_replay_with_new_plan(kernel):
     """Capture once with a fixed grid, re-plan (different lengths), replay."""
     c = Case(seq_lens=(900, 40, 2100), h_q=16, h_k=2, kv_format="fp8", seed=13, max_num_seqs=4)
-    r = c.runner()
+    r = c.runner(kernel=kernel)
     T = c.b
     out = torch.zeros(T, c.h_q * c.d, dtype=torch.float32, device="cuda")
     kd, vd = c.dev(c.kd), c.dev(c.vd)
@@ -141,7 +163,8 @@ def test_graph_replay_with_new_plan():
     assert_close_fp32(out.view(T, c.h_q, c.d), ref, what="graph replay")
 
 
-def test_bad_page_sets_status_not_fault():
+@pytest.mark.parametrize("kernel", ["simt", "tc"])
+def test_bad_page_sets_status_not_fault(kernel):
     """A block-table entry past the pool is flagged in the status word and
     skipped (no out-of-bounds read)."""
     from mjolnir_b200 import _lib
@@ -149,4 +172,38 @@ def test_bad_page_sets_status_not_fault():
     c = Case(seq_lens=(100,), h_q=8, h_k=2, kv_format="fp8", seed=17)
     c.block_table[0, 1] = c.num_pages + 5  # in bounds of the table, out of the pool
     with pytest.raises(_lib.MjolnirError):
-        c.run()
+        c.run(kernel=kernel)
+
+
+@pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
+@pytest.mark.parametrize("page_size", [16, 32, 64, 128])
+def test_tc_page_sizes(kv_format, page_size):
+    lens = (1, 127, 128, 129, 1000, 4097)
+    c = Case(seq_lens=lens, h_q=32, h_k=4, page_size=page_size, kv_format=kv_format, layout="BHN2D", seed=page_size)
+    out, _, _ = c.run(kernel="tc")
+    ref, _ = c.oracle()
+    T = c.b
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"tc {kv_format} PS {page_size}")
+
+
+def test_tc_nan_bytes_past_sequence_end():
+    """fp8 rows after the last token of a sequence's last page may hold NaN
+    bytes (0x7F); they get P = 0 and must not reach O."""
+    c = Case(seq_lens=(37, 200), h_q=8, h_k=2, kv_format="fp8", layout="BHN2D", seed=31)
+    for s, L in enumerate(c.seq_lens):
+        page = int(c.block_table_cpu[s, (L - 1) // c.PS])
+        c.k_view[page, L % c.PS:] = 0x7F
+        c.v_view[page, L % c.PS:] = 0x7F
+    out, _, _ = c.run(kernel="tc")
+    ref, _ = c.oracle()
+    assert_close_fp32(out[: c.b].view(c.b, c.h_q, c.d), ref, what="nan tail")
+
+
+def test_tc_zero_length_padding_request():
+    """A CUDA-graph padding request (seq_len 0) writes O = 0, nothing else moves."""
+    c = Case(seq_lens=(300, 0, 50), h_q=8, h_k=2, kv_format="e2m3", layout="BHN2D", seed=33)
+    out, _, _ = c.run(kernel="tc")
+    ref, _ = c.oracle()
+    got = out[: c.b].view(c.b, c.h_q, c.d)
+    assert (got[1] == 0).all()
+    assert_close_fp32(got, ref, what="padding request")
