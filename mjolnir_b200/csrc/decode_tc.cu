@@ -62,30 +62,30 @@ constexpr int kWarpSm0 = 4;    // warps 4-7: softmax warpgroup
 
 template <int FMT, int NQP>
 struct Cfg {
-  static constexpr int N = 3 * NQP;                       // MMA N: hi, mid, lo row blocks
-  static constexpr int STAGES = (FMT == MJ_KV_E2M3) ? 2 : 3;
+  // MMA N: three row blocks (hi, mid, lo) of NQP rows, padded to 16
+  static constexpr int N = (3 * NQP) < 16 ? 16 : 3 * NQP;
+  static constexpr int QBYTES = N * 128;                  // one K-major Q or P operand
+  static constexpr int STAGES = (FMT == MJ_KV_E2M3) ? 2 : (NQP <= 8 ? 3 : 2);
   static constexpr int TMEM_COLS = (4 * N) <= 32 ? 32 : (4 * N) <= 64 ? 64 : (4 * N) <= 128 ? 128 : 256;
   static_assert(4 * N <= 256, "two CTAs per SM share the 512 TMEM columns");
-  static constexpr uint32_t TX_BYTES = (FMT == MJ_KV_E2M3) ? 2u * 128u * 96u : 2u * 128u * 128u;
+  static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
   // shared memory plan (offsets from a 1024-aligned base)
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + STAGES * kTileBytes;
-  static constexpr int VC_OFF = V_OFF + STAGES * kTileBytes;               // e2m3 converted V ring (2)
-  static constexpr int Q_OFF = VC_OFF + ((FMT == MJ_KV_E2M3) ? 2 * kTileBytes : 0);
-  static constexpr int P_OFF = Q_OFF + N * 128;                            // P ring (2)
-  static constexpr int BAR_OFF = P_OFF + 2 * N * 128;
-  static constexpr int NBARS = 2 * STAGES + 2 * 7 + 2;  // full/empty, 7 pairs, q_full, drain
-  static constexpr int RED_OFF = BAR_OFF + NBARS * 8;    // float red[2][4][NQP]
+  static constexpr int VC_OFF = V_OFF + STAGES * kTileBytes;  // e2m3: converted V, two slots
+  static constexpr int Q_OFF = VC_OFF + ((FMT == MJ_KV_E2M3) ? 2 * kTileBytes : 0);  // two slots (jobs)
+  static constexpr int P_OFF = Q_OFF + 2 * QBYTES;                                  // two slots (tiles)
+  static constexpr int BAR_OFF = P_OFF + 2 * QBYTES;
+  static constexpr int NBARS = 4 * STAGES + 2 * 8 + 1;  // k/v full/empty rings, 8 pairs, drain
+  static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[2][4][NQP]
   static constexpr int LIM_OFF = RED_OFF + 2 * 4 * NQP * 4;  // int lim[NQP]
-  static constexpr int MISC_OFF = LIM_OFF + NQP * 4;     // tmem base, abort flag, l/m scratch
+  static constexpr int MISC_OFF = LIM_OFF + NQP * 4;    // tmem base, abort flag, l scratch [4][NQP]
   static constexpr int SMEM = MISC_OFF + 64 + 4 * 4 * NQP + 1024;  // + alignment slack
 };
 
 struct Bars {
-  uint64_t* full;
-  uint64_t* empty;
-  uint64_t *s_full, *s_free, *p_full, *o_full, *o_free, *v_ready, *v_free;
-  uint64_t* q_full;
+  uint64_t *k_full, *k_empty, *v_full, *v_empty;               // TMA rings
+  uint64_t *s_full, *s_free, *p_full, *o_full, *o_free, *v_ready, *v_free, *q_full;  // pairs
   uint64_t* drain;
 };
 
@@ -131,7 +131,7 @@ __device__ __forceinline__ void store_split(unsigned char* buf, int r, int t, ui
 // 3*NQP TMEM columns of this thread's lane -> v
 template <int NQP>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
-  constexpr int C = 3 * NQP;
+  constexpr int C = (3 * NQP) < 16 ? 16 : 3 * NQP;
 #pragma unroll
   for (int c = 0; c + 16 <= C; c += 16) tmem_ld16(taddr + c, v + c);
   if (C % 16) tmem_ld8(taddr + (C / 16) * 16, v + (C / 16) * 16);
@@ -158,19 +158,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const int4 wi = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
-  const int seq = wi.x, tb = wi.y, te = wi.z, split = wi.w;
-  if (tb >= te) return;  // empty (padding) item: uniform exit before any barrier
-  const int h = blockIdx.y;
-  const int L = a.seq_lens[seq];
-  const int n_tiles = te - tb;
+  const int h_k = a.h_k;
+  const int total_jobs = a.num_work * h_k;  // job p: work item p / h_k, KV head p % h_k
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
   Bars b;
-  b.full = bars;
-  b.empty = bars + S;
-  b.s_full = bars + 2 * S;
+  b.k_full = bars;
+  b.k_empty = bars + S;
+  b.v_full = bars + 2 * S;
+  b.v_empty = bars + 3 * S;
+  b.s_full = bars + 4 * S;
   b.s_free = b.s_full + 2;
   b.p_full = b.s_free + 2;
   b.o_full = b.p_full + 2;
@@ -178,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   b.v_ready = b.o_free + 2;
   b.v_free = b.v_ready + 2;
   b.q_full = b.v_free + 2;
-  b.drain = b.q_full + 1;
+  b.drain = b.q_full + 2;
   float* red = reinterpret_cast<float*>(sm + C::RED_OFF);   // [2][4][NQP]
   int* lim_s = reinterpret_cast<int*>(sm + C::LIM_OFF);      // [NQP]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::MISC_OFF);
@@ -188,8 +185,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&b.full[i], 1);
-      mbar_init(&b.empty[i], 1);
+      mbar_init(&b.k_full[i], 1);
+      mbar_init(&b.k_empty[i], 1);
+      mbar_init(&b.v_full[i], 1);
+      // e2m3: the converter warps release the raw V slot; e4m3: the PV MMA does
+      mbar_init(&b.v_empty[i], FMT == MJ_KV_E2M3 ? 64 : 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b.s_full[i], 1);
@@ -199,8 +199,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&b.o_free[i], 128);
       mbar_init(&b.v_ready[i], 64);
       mbar_init(&b.v_free[i], 1);
+      mbar_init(&b.q_full[i], 1);
     }
-    mbar_init(b.q_full, 1);
     mbar_init(b.drain, 1);
     *abort_flag = 0;
     never_abort = 0;
@@ -222,263 +222,310 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto kbuf = [&](int st) { return sm + C::K_OFF + st * kTileBytes; };
   auto vbuf = [&](int st) { return sm + C::V_OFF + st * kTileBytes; };
   auto vcvt = [&](int i) { return sm + C::VC_OFF + i * kTileBytes; };
-  unsigned char* qbuf = sm + C::Q_OFF;
-  auto pbuf = [&](int i) { return sm + C::P_OFF + i * N * 128; };
+  auto qbuf = [&](int i) { return sm + C::Q_OFF + i * C::QBYTES; };
+  auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::QBYTES; };
   auto give_up = [&]() {
     *abort_flag = 1;
     flag(a.status, MJ_DEV_TIMEOUT);
+  };
+  // every role walks the same job list and skips the same empty items
+  auto job = [&](int p, int& seq, int& tb, int& te, int& split, int& h) {
+    const int4 wi = reinterpret_cast<const int4*>(a.work)[p / h_k];
+    seq = wi.x;
+    tb = wi.y;
+    te = wi.z;
+    split = wi.w;
+    h = p % h_k;
+    return te > tb;
   };
 
   if (warp == kWarpTma) {
     // ---------------------------------------------------------------- producer
     const int PS = a.page_size;
     const int P = kTileRows / PS;  // pages per tile; lane p < P loads page p
-    const int32_t* bt = a.block_table + (int64_t)seq * a.block_table_stride;
-    auto page_coord = [&](int i) {
-      int pg = (int)a.num_pages;  // out of range -> the TMA zero-fills the box
-      const int row0 = (tb + i) * kTileRows + lane * PS;
-      if (lane < P && row0 < L) {
-        const int v = bt[row0 / PS];
-        if (v < 0 || (int64_t)v >= a.num_pages) {
-          flag(a.status, MJ_DEV_BAD_PAGE);
-        } else {
-          pg = v;
+    int it = 0, k_issued = 0, v_issued = 0;
+    bool ok = true;
+    for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
+      int seq, tb, te, split, h;
+      if (!job(p, seq, tb, te, split, h)) continue;
+      const int L = a.seq_lens[seq];
+      const int32_t* bt = a.block_table + (int64_t)seq * a.block_table_stride;
+      auto page_coord = [&](int tile) {
+        int pg = (int)a.num_pages;  // out of range -> the TMA zero-fills the box
+        const int row0 = tile * kTileRows + lane * PS;
+        if (lane < P && row0 < L) {
+          const int v = bt[row0 / PS];
+          if (v < 0 || (int64_t)v >= a.num_pages) flag(a.status, MJ_DEV_BAD_PAGE);
+          else pg = v;
         }
+        return pg;
+      };
+      int pg_next = page_coord(tb);
+      for (int tile = tb; tile < te; ++tile, ++it) {
+        const int st = it % S;
+        const uint32_t par = ((it / S) & 1) ^ 1;
+        const int pg = pg_next;
+        if (tile + 1 < te) pg_next = page_coord(tile + 1);
+        if (lane == 0) ok = mbar_wait(&b.k_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], C::K_TX);
+        __syncwarp();
+        if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg);
+        k_issued = it + 1;
+        if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], C::K_TX);
+        __syncwarp();
+        if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg);
+        v_issued = it + 1;
       }
-      return pg;
-    };
-    int pg_next = page_coord(0);
-    int issued = 0;
-    for (int i = 0; i < n_tiles; ++i) {
-      const int st = i % S;
-      const int pg = pg_next;
-      if (i + 1 < n_tiles) pg_next = page_coord(i + 1);
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&b.empty[st], ((i / S) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0 && !*abort_flag) give_up();
-        break;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&b.full[st], C::TX_BYTES);
-      __syncwarp();
-      if (lane < P) {
-        tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.full[st], 0, 0, h, pg);
-        tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.full[st], 0, 0, h, pg);
-      }
-      issued = i + 1;
     }
-    // every issued copy must land before the CTA may exit
-    if (lane == 0 && *abort_flag) {
-      for (int k = issued > S ? issued - S : 0; k < issued; ++k)
-        mbar_wait(&b.full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
+    if (lane == 0) {
+      if (!ok && !*abort_flag) give_up();
+      if (*abort_flag) {  // every issued copy must land before the CTA may exit
+        for (int k = k_issued > S ? k_issued - S : 0; k < k_issued; ++k)
+          mbar_wait(&b.k_full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
+        for (int k = v_issued > S ? v_issued - S : 0; k < v_issued; ++k)
+          mbar_wait(&b.v_full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
+      }
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(b.q_full, 0, abort_flag, MJ_TC_WAIT_NS);
       const uint32_t idesc_s = idesc_f8f6f4(FMT == MJ_KV_E2M3 ? 3u : 0u, 0u, 0u, 0u, (uint32_t)N);
       const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 0u, (uint32_t)N);
-      const uint32_t qaddr = smem_addr(qbuf);
-      for (int i = 0; ok && i <= n_tiles; ++i) {
-        if (i < n_tiles) {  // S_i = K_i . Q^T
-          const int st = i % S;
-          ok = mbar_wait(&b.full[st], (i / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-               mbar_wait(&b.s_free[i & 1], ((i >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+      bool ok = true;
+      int it = 0, jc = 0;
+      // O_t^T = V_t^T . P_t^T for global tile t
+      auto pv = [&](int t) {
+        const int st = t % S;
+        if (!(mbar_wait(&b.p_full[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+              mbar_wait(&b.v_ready[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+              mbar_wait(&b.o_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)))
+          return false;
+        tc_fence_after();
+        const uint32_t vaddr = smem_addr(FMT == MJ_KV_E2M3 ? vcvt(t & 1) : vbuf(st));
+        const uint32_t paddr = smem_addr(pbuf(t & 1));
+        const uint32_t d = tmem + (uint32_t)(2 * N + (t & 1) * N);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f8f6f4(d, smem_desc_sw128(vaddr + 4096 * k, kTileBytes, 1024), smem_desc_sw128(paddr + 32 * k, 16, 1024),
+                     idesc_o, k > 0);
+        mma_commit(&b.o_full[t & 1]);
+        if (FMT != MJ_KV_E2M3) mma_commit(&b.v_empty[st]);
+        mma_commit(&b.v_free[t & 1]);
+        return true;
+      };
+      for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
+        int seq, tb, te, split, h;
+        if (!job(p, seq, tb, te, split, h)) continue;
+        ok = mbar_wait(&b.q_full[jc & 1], (jc >> 1) & 1, abort_flag, MJ_TC_WAIT_NS);
+        const uint32_t qaddr = smem_addr(qbuf(jc & 1));
+        ++jc;
+        const int n = te - tb;
+        for (int i = 0; ok && i < n; ++i, ++it) {  // S_i = K_i . Q^T, then PV of the tile before
+          const int st = it % S;
+          ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+               mbar_wait(&b.s_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
           if (!ok) break;
           tc_fence_after();
           const uint32_t kaddr = smem_addr(kbuf(st));
-          const uint32_t d = tmem + (uint32_t)((i & 1) * N);
+          const uint32_t d = tmem + (uint32_t)((it & 1) * N);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, 1024), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
                        idesc_s, k > 0);
-          mma_commit(&b.s_full[i & 1]);
+          mma_commit(&b.s_full[it & 1]);
+          mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
+          if (i >= 1) ok = pv(it - 1);
         }
-        if (i >= 1) {  // O_j^T = V_j^T . P_j^T for the previous tile
-          const int j = i - 1, st = j % S;
-          ok = mbar_wait(&b.p_full[j & 1], (j >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-               mbar_wait(&b.v_ready[j & 1], (j >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-               mbar_wait(&b.o_free[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t vaddr = smem_addr(FMT == MJ_KV_E2M3 ? vcvt(j & 1) : vbuf(st));
-          const uint32_t paddr = smem_addr(pbuf(j & 1));
-          const uint32_t d = tmem + (uint32_t)(2 * N + (j & 1) * N);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f8f6f4(d, smem_desc_sw128(vaddr + 4096 * k, kTileBytes, 1024),
-                       smem_desc_sw128(paddr + 32 * k, 16, 1024), idesc_o, k > 0);
-          mma_commit(&b.o_full[j & 1]);
-          mma_commit(&b.empty[st]);
-          mma_commit(&b.v_free[j & 1]);
-        }
+        if (ok) ok = pv(it - 1);  // the job's last tile
       }
       if (!ok && !*abort_flag) give_up();
-      // all issued MMAs must complete before TMEM is released
-      mma_commit(b.drain);
+      mma_commit(b.drain);  // all issued MMAs complete before TMEM is released
       mbar_wait(b.drain, 0, &never_abort, MJ_TC_WAIT_NS);
     }
     __syncwarp();
   } else if (warp < kWarpSm0) {
     // ------------------------------------------------ V conversion / tail zero
     const int ct = threadIdx.x - kWarpCvt0 * 32;  // 0..63
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j % S;
-      // v_free bounds this role to two tiles ahead of the PV MMA: v_ready is a
-      // two-slot barrier pair, and running further ahead would complete a
-      // phase the MMA has not waited for yet
-      bool ok = mbar_wait(&b.full[st], (j / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-                mbar_wait(&b.v_free[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
-      if (!ok) {
-        if (!*abort_flag) give_up();
-        break;
-      }
-      if (FMT == MJ_KV_E2M3) {
-        const uint4* src = reinterpret_cast<const uint4*>(vbuf(st));
-        uint4* dst = reinterpret_cast<uint4*>(vcvt(j & 1));
+    int it = 0;
+    bool ok = true;
+    for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
+      int seq, tb, te, split, h;
+      if (!job(p, seq, tb, te, split, h)) continue;
+      const int L = a.seq_lens[seq];
+      for (int tile = tb; tile < te; ++tile, ++it) {
+        const int st = it % S;
+        // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
+        ok = mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+             mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+        if (!ok) break;
+        if (FMT == MJ_KV_E2M3) {
+          const uint4* src = reinterpret_cast<const uint4*>(vbuf(st));
+          uint4* dst = reinterpret_cast<uint4*>(vcvt(it & 1));
 #pragma unroll 4
-        for (int c = ct; c < kTileBytes / 16; c += 64) dst[c] = e2m3x16_to_e4m3(src[c]);
-        // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
-      } else {
-        // e4m3 rows past the sequence end inside its last page may hold NaN
-        // bytes; NaN * 0 would poison O, so zero them (their P is 0)
-        const int valid = L - (tb + j) * kTileRows;
-        if (valid < kTileRows) {
-          const int r0 = valid > 0 ? valid : 0;
-          uint4* v4 = reinterpret_cast<uint4*>(vbuf(st));
-          for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64) v4[c] = make_uint4(0, 0, 0, 0);
+          for (int c = ct; c < kTileBytes / 16; c += 64) dst[c] = e2m3x16_to_e4m3(src[c]);
+          // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
+          mbar_arrive(&b.v_empty[st]);  // raw V slot free for the next TMA
+        } else {
+          // e4m3 rows past the sequence end inside its last page may hold NaN
+          // bytes; NaN * 0 would poison O, so zero them (their P is 0)
+          const int valid = L - tile * kTileRows;
+          if (valid < kTileRows) {
+            const int r0 = valid > 0 ? valid : 0;
+            uint4* v4 = reinterpret_cast<uint4*>(vbuf(st));
+            for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64) v4[c] = make_uint4(0, 0, 0, 0);
+          }
         }
+        fence_proxy_async_smem();
+        mbar_arrive(&b.v_ready[it & 1]);
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&b.v_ready[j & 1]);
     }
+    if (!ok && !*abort_flag) give_up();
   } else {
     // --------------------------------------------------- softmax warpgroup
     const int t = threadIdx.x - kWarpSm0 * 32;  // 0..127: TMEM lane = KV row of a tile = head-dim index
     const int wq = warp - kWarpSm0;             // TMEM lane quarter
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const int h_k = a.h_k, h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r;
-
-    // Q: this thread holds head-dim element t of every query row
-    float qv[NQP];
-    float qmax = 0.f;
-#pragma unroll
-    for (int r = 0; r < NQP; ++r) {
-      float x = 0.f;
-      if (r < n_q) {
-        const int qi = r / h_r, rr = r % h_r;
-        const int64_t tok = (int64_t)seq * q_len + qi;
-        const int qh = h * h_r + rr;
-        x = load_elem(a.q, tok * a.q_stride_tok + qh * a.q_stride_head + t, a.q_dtype);
-        if (a.q_mul) x *= a.q_mul[(int64_t)qh * 128 + t];
+    const int h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r;
+    // padding rows of the Q and P operands (past 3*NQP) stay zero for the whole kernel
+    for (int i = 0; i < 2; ++i)
+      for (int row = 3 * NQP; row < N; ++row) {
+        qbuf(i)[sw128_offset(row, t)] = 0;
+        pbuf(i)[sw128_offset(row, t)] = 0;
       }
-      qv[r] = x;
-      qmax = fmaxf(qmax, fabsf(x));
-    }
-    qmax = warp_max_f32(qmax);
-    if (lane == 0) red[wq] = qmax;
-    if (t < NQP) lim_s[t] = (t < n_q) ? (a.causal ? L - q_len + t / h_r : L - 1) : -1;
-    named_bar_sync(1, 128);
-    qmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    // three-term e4m3 split of q * qs, |q * qs| <= 224
-    const float qs = qmax > 0.f ? 224.f / qmax : 1.f;
-#pragma unroll
-    for (int r = 0; r < NQP; r += 2) {
-      uint16_t hb, mb, lb;
-      split3(qv[r] * qs, qv[r + 1] * qs, hb, mb, lb);
-      store_split<NQP>(qbuf, r, t, hb, mb, lb);
-    }
-    fence_proxy_async_smem();
-    const float kd = descale_at(a.k_descale, a.k_descale_mode, seq, h, h_k);
-    const float vd = descale_at(a.v_descale, a.v_descale_mode, seq, h, h_k);
-    const float c2 = a.softmax_scale * kd * kLog2e / qs;  // S (in q*qs units) -> log2 units
-    named_bar_sync(1, 128);  // all Q bytes written and fenced; red[] reads done
-    if (t == 0) mbar_arrive(b.q_full);
-
-    float m[NQP], l[NQP], cr[NQP], oacc[NQP];
-#pragma unroll
-    for (int r = 0; r < NQP; ++r) {
-      m[r] = -INFINITY;
-      l[r] = 0.f;
-      cr[r] = 1.f;
-      oacc[r] = 0.f;
-    }
-    // fold the O tile of KV tile jj into the register accumulator
-    auto fold = [&](int jj) {
-      if (!mbar_wait(&b.o_full[jj & 1], (jj >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
-      tc_fence_after();
-      float ov[3 * NQP];
-      tmem_ld_cols<NQP>(tmem + (uint32_t)(2 * N + (jj & 1) * N) + lane_base, ov);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&b.o_free[jj & 1]);
-#pragma unroll
-      for (int r = 0; r < NQP; ++r) oacc[r] = fmaf(oacc[r], cr[r], combine3<NQP>(ov, r));
-    };
-
+    int it = 0, jc = 0;
     bool aborted = false;
-    for (int i = 0; i < n_tiles; ++i) {
-      if (i >= 1) fold(i - 1);  // uses cr of tile i-1
-      if (!mbar_wait(&b.s_full[i & 1], (i >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
-      tc_fence_after();
-      float sv[3 * NQP];
-      tmem_ld_cols<NQP>(tmem + (uint32_t)((i & 1) * N) + lane_base, sv);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&b.s_free[i & 1]);
-      const int j = (tb + i) * kTileRows + t;  // this thread's KV row
-      float* rd = red + (i & 1) * 4 * NQP;
+    for (int p = blockIdx.x; !aborted && p < total_jobs; p += gridDim.x) {
+      int seq, tb, te, split, h;
+      if (!job(p, seq, tb, te, split, h)) continue;
+      const int L = a.seq_lens[seq];
+      // ---- Q of this job: head-dim element t of every query row, split in 3 e4m3 terms
+      float qv[NQP];
+      float qmax = 0.f;
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
-        float s = combine3<NQP>(sv, r) * c2;
-        if (j > lim_s[r]) s = -INFINITY;
-        sv[r] = s;
-        const float wm = warp_max_f32(s);
-        if (lane == 0) rd[wq * NQP + r] = wm;
+        float x = 0.f;
+        if (r < n_q) {
+          const int qi = r / h_r, rr = r % h_r;
+          const int64_t tok = (int64_t)seq * q_len + qi;
+          const int qh = h * h_r + rr;
+          x = load_elem(a.q, tok * a.q_stride_tok + qh * a.q_stride_head + t, a.q_dtype);
+          if (a.q_mul) x *= a.q_mul[(int64_t)qh * 128 + t];
+        }
+        qv[r] = x;
+        qmax = fmaxf(qmax, fabsf(x));
       }
-      // the max exchange barrier doubles as a uniform abort vote
+      qmax = warp_max_f32(qmax);
+      if (lane == 0) red[wq] = qmax;
+      if (t < NQP) lim_s[t] = (t < n_q) ? (a.causal ? L - q_len + t / h_r : L - 1) : -1;
+      if (named_bar_or(1, 128, *abort_flag != 0)) break;
+      qmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+      const float qs = qmax > 0.f ? 224.f / qmax : 1.f;  // |q * qs| <= 224
+      unsigned char* qb = qbuf(jc & 1);
+#pragma unroll
+      for (int r = 0; r < NQP; r += 2) {
+        uint16_t hb, mb, lb;
+        split3(qv[r] * qs, qv[r + 1] * qs, hb, mb, lb);
+        store_split<NQP>(qb, r, t, hb, mb, lb);
+      }
+      fence_proxy_async_smem();
+      const float kd = descale_at(a.k_descale, a.k_descale_mode, seq, h, h_k);
+      const float vd = descale_at(a.v_descale, a.v_descale_mode, seq, h, h_k);
+      const float c2 = a.softmax_scale * kd * kLog2e / qs;  // S (in q*qs units) -> log2 units
+      if (named_bar_or(1, 128, *abort_flag != 0)) break;  // Q written and fenced, red[] read
+      if (t == 0) mbar_arrive(&b.q_full[jc & 1]);
+      ++jc;
+
+      float m[NQP], l[NQP], cr[NQP], oacc[NQP];
+#pragma unroll
+      for (int r = 0; r < NQP; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+        cr[r] = 1.f;
+        oacc[r] = 0.f;
+      }
+      // fold the O tile of global tile tt into the register accumulator (uses cr of that tile)
+      auto fold = [&](int tt) {
+        if (!mbar_wait(&b.o_full[tt & 1], (tt >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
+        tc_fence_after();
+        float ov[N];
+        tmem_ld_cols<NQP>(tmem + (uint32_t)(2 * N + (tt & 1) * N) + lane_base, ov);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&b.o_free[tt & 1]);
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) oacc[r] = fmaf(oacc[r], cr[r], combine3<NQP>(ov, r));
+      };
+
+      const int n = te - tb;
+      for (int i = 0; i < n; ++i, ++it) {
+        if (i >= 1) fold(it - 1);
+        if (!mbar_wait(&b.s_full[it & 1], (it >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
+        tc_fence_after();
+        float sv[N];
+        tmem_ld_cols<NQP>(tmem + (uint32_t)((it & 1) * N) + lane_base, sv);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&b.s_free[it & 1]);
+        const int j = (tb + i) * kTileRows + t;  // this thread's KV row
+        float* rd = red + (it & 1) * 4 * NQP;
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) {
+          float s = combine3<NQP>(sv, r) * c2;
+          if (j > lim_s[r]) s = -INFINITY;
+          sv[r] = s;
+          const float wm = warp_max_f32(s);
+          if (lane == 0) rd[wq * NQP + r] = wm;
+        }
+        // the max exchange barrier doubles as a uniform abort vote
+        if (named_bar_or(1, 128, *abort_flag != 0)) {
+          aborted = true;
+          break;
+        }
+        unsigned char* pb = pbuf(it & 1);
+#pragma unroll
+        for (int r = 0; r < NQP; r += 2) {
+          float p2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int rr = r + u;
+            const float mt = fmaxf(fmaxf(rd[rr], rd[NQP + rr]), fmaxf(rd[2 * NQP + rr], rd[3 * NQP + rr]));
+            const float m_new = fmaxf(m[rr], mt);
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            const float corr = exp2f(m[rr] - m_use);  // m = -inf -> 0
+            const float pv = exp2f(sv[rr] - m_use);   // masked -> 0
+            l[rr] = fmaf(l[rr], corr, pv);
+            m[rr] = m_new;
+            cr[rr] = corr;
+            p2[u] = pv * kPScale;
+          }
+          uint16_t hb, mb, lb;
+          split3(p2[0], p2[1], hb, mb, lb);
+          store_split<NQP>(pb, r, t, hb, mb, lb);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&b.p_full[it & 1]);
+      }
+      if (aborted) break;
+      fold(it - 1);
+
+      // ---- epilogue: l per query row (sum of the per-thread partials), outputs
+#pragma unroll
+      for (int r = 0; r < NQP; ++r) {
+        float x = l[r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        if (lane == 0) lred[wq * NQP + r] = x;
+      }
       if (named_bar_or(1, 128, *abort_flag != 0)) {
         aborted = true;
         break;
       }
-      unsigned char* pb = pbuf(i & 1);
-#pragma unroll
-      for (int r = 0; r < NQP; r += 2) {
-        float p2[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int rr = r + u;
-          const float mt = fmaxf(fmaxf(rd[rr], rd[NQP + rr]), fmaxf(rd[2 * NQP + rr], rd[3 * NQP + rr]));
-          const float m_new = fmaxf(m[rr], mt);
-          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-          const float corr = exp2f(m[rr] - m_use);  // m = -inf -> 0
-          const float p = exp2f(sv[rr] - m_use);    // masked -> 0
-          l[rr] = fmaf(l[rr], corr, p);
-          m[rr] = m_new;
-          cr[rr] = corr;
-          p2[u] = p * kPScale;
-        }
-        uint16_t hb, mb, lb;
-        split3(p2[0], p2[1], hb, mb, lb);
-        store_split<NQP>(pb, r, t, hb, mb, lb);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&b.p_full[i & 1]);
-    }
-    if (!aborted) fold(n_tiles - 1);
-
-    // l: per-thread partial sums over this thread's KV rows -> per query row
-#pragma unroll
-    for (int r = 0; r < NQP; ++r) {
-      float x = l[r];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-      if (lane == 0) lred[wq * NQP + r] = x;
-    }
-    aborted = named_bar_or(1, 128, aborted || *abort_flag != 0);
-    if (!aborted) {
       const bool final_out = a.n_splits[seq] <= 1;
       const float vscale = (FMT == MJ_KV_E2M3 ? 64.f : 1.f) * vd / kPScale;
       if (!final_out && (split >= a.max_splits || seq >= a.part_seqs || !a.o_part)) {
@@ -577,17 +624,41 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t s_page, int64_t s
   return r == CUDA_SUCCESS;
 }
 
+// Persistent launch: one CTA per resident slot (SMs x CTAs per SM), each walking
+// the job list (work item, KV head) with a stride of the grid size. The work
+// list is longest-first, so the round-robin is a longest-first assignment.
 template <int FMT, int NQP>
 static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream) {
   const int smem = tc::Cfg<FMT, NQP>::SMEM;
-  static bool attr_done = false;
-  if (!attr_done) {
+  static int slots = 0;  // resident CTAs on this device (set once: one process per GPU)
+  if (!slots) {
     cudaError_t e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    // without a carveout preference the occupancy is computed for a smaller
+    // shared-memory partition and one CTA per SM would be assumed
+    e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    // resident CTAs per SM from the device limits: shared memory (with the
+    // per-block reserve), registers, and the 512 TMEM columns of an SM
+    int dev = 0, sms = 0, smem_sm = 0, reserve = 0, regs_sm = 0;
+    cudaFuncAttributes fa;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&reserve, cudaDevAttrReservedSharedMemoryPerBlock, dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&fa, tc::decode_tc_kernel<FMT, NQP>)) != cudaSuccess) return e;
+    int occ = smem_sm / (smem + (int)fa.sharedSizeBytes + reserve);
+    const int regs_cta = ((fa.numRegs + 7) / 8) * 8 * tc::kThreads;
+    occ = occ < regs_sm / regs_cta ? occ : regs_sm / regs_cta;
+    occ = occ < 512 / tc::Cfg<FMT, NQP>::TMEM_COLS ? occ : 512 / tc::Cfg<FMT, NQP>::TMEM_COLS;
+    occ = occ < 2 ? occ : 2;  // __launch_bounds__ min blocks
+    slots = sms * (occ > 0 ? occ : 1);
   }
-  dim3 grid((unsigned)a.num_work, (unsigned)a.h_k);
+  const int64_t jobs = (int64_t)a.num_work * a.h_k;
+  const unsigned grid = (unsigned)(jobs < slots ? jobs : slots);
   tc::decode_tc_kernel<FMT, NQP><<<grid, tc::kThreads, smem, stream>>>(a, mk, mv);
   return cudaGetLastError();
 }
@@ -603,8 +674,11 @@ cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool*
     return cudaErrorInvalidValue;
   *handled = true;
   const int n_q = a.q_len * (a.h_q / a.h_k);
-  if (a.kv_format == MJ_KV_E2M3)
+  if (a.kv_format == MJ_KV_E2M3) {
+    if (n_q <= 4) return launch_tc_t<MJ_KV_E2M3, 4>(a, mk, mv, stream);
     return n_q <= 8 ? launch_tc_t<MJ_KV_E2M3, 8>(a, mk, mv, stream) : launch_tc_t<MJ_KV_E2M3, 16>(a, mk, mv, stream);
+  }
+  if (n_q <= 4) return launch_tc_t<MJ_KV_FP8_E4M3, 4>(a, mk, mv, stream);
   return n_q <= 8 ? launch_tc_t<MJ_KV_FP8_E4M3, 8>(a, mk, mv, stream) : launch_tc_t<MJ_KV_FP8_E4M3, 16>(a, mk, mv, stream);
 }
 
