@@ -69,13 +69,15 @@ def kv_bytes(lens, h_k, d, kv):
 class Workload:
     """One rank's shard of a workload, resident on the device."""
 
-    def __init__(self, name, kv, rank, world, device, seed=1234):
+    def __init__(self, name, kv, rank, world, device, seed=1234, page_size=None):
         from mjolnir_b200 import kvfp6
         from mjolnir_b200.runner import DecodeRunner, split_kv_cache
 
         w = dict(WORKLOADS[name])
         if kv:
             w["kv"] = kv
+        if page_size:
+            w["PS"] = page_size
         self.w, self.name = w, name
         if w["h_k"] % world:
             raise SystemExit(f"{w['h_k']} KV heads do not shard over {world} GPUs")
@@ -322,6 +324,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
     ap.add_argument("--kv", default=None, choices=[None, "fp8", "e2m3"])
+    ap.add_argument("--page-size", type=int, default=None, help="override the workload's KV page size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -343,7 +346,7 @@ def main():
     from mjolnir_b200 import _lib, kvfp6
     from mjolnir_b200.runner import _stream
 
-    wl = Workload(args.workload, args.kv, rank, world, dev)
+    wl = Workload(args.workload, args.kv, rank, world, dev, page_size=args.page_size)
     stream = _stream(dev)
     cw = kvfp6.cache_write_args(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt)
     da = wl.runner.decode_args(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale,

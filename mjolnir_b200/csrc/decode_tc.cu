@@ -21,9 +21,9 @@
 //                      A = V (e4m3, MN-major), B = P; a fresh TMEM tile per KV
 //                      tile, folded into fp32 registers (thread = head-dim
 //                      lane) with the running-max correction
-//   e2m3 V cannot be an MN-major MMA operand, so two converter warps turn each
-//   16-code chunk into 16 e4m3 bytes of value code * 2^-6 (exact; the 2^6 is
-//   folded into the output scale) at the same swizzled offset.
+//   e2m3 V cannot be an MN-major MMA operand, so two converter warps rewrite
+//   each 16-code slot in place as 16 e4m3 bytes of value code * 2^-6 (exact;
+//   the 2^6 is folded into the output scale).
 //
 // Numerics: split-fp8 Q and P carry ~12 significant bits each
 // (hi + mid / 16 + lo / 256),
@@ -52,7 +52,11 @@ constexpr int kThreads = 256;   // 8 warps
 constexpr int kTileBytes = 128 * 128;  // one 128 x 128 byte operand tile (e2m3: 16U6 slots)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr float kPScale = 448.0f;  // P (<= 1) is stored as e4m3(p * 448) hi/lo
+// The running max is raised only when a score exceeds it by more than
+// 2^kRescaleLog2 (the rest of the time no cross-thread max is needed), so
+// p <= 2^kRescaleLog2 and p * kPScale <= 448 fits e4m3.
+constexpr float kRescaleLog2 = 8.0f;
+constexpr float kPScale = 448.0f / 256.0f;
 
 // warp roles
 constexpr int kWarpTma = 0;
@@ -62,25 +66,26 @@ constexpr int kWarpSm0 = 4;    // warps 4-7: softmax warpgroup
 
 template <int FMT, int NQP>
 struct Cfg {
-  // MMA N: three row blocks (hi, mid, lo) of NQP rows, padded to 16
-  static constexpr int N = (3 * NQP) < 16 ? 16 : 3 * NQP;
-  static constexpr int QBYTES = N * 128;                  // one K-major Q or P operand
-  static constexpr int STAGES = (FMT == MJ_KV_E2M3) ? 2 : (NQP <= 8 ? 3 : 2);
-  static constexpr int TMEM_COLS = (4 * N) <= 32 ? 32 : (4 * N) <= 64 ? 64 : (4 * N) <= 128 ? 128 : 256;
-  static_assert(4 * N <= 256, "two CTAs per SM share the 512 TMEM columns");
+  // Query rows enter the MMAs as three row blocks (hi, mid, lo) of NQP rows.
+  static constexpr int NS = (3 * NQP + 7) / 8 * 8 < 16 ? 16 : (3 * NQP + 7) / 8 * 8;  // S MMA N (Q is K-major)
+  static constexpr int NO = (3 * NQP + 15) / 16 * 16;    // PV MMA N (P is MN-major: multiples of 16)
+  static constexpr int QBYTES = NS * 128;                // one K-major Q operand
+  static constexpr int PBYTES = NO * 128;                // one MN-major P operand: NO/16 groups of [128 s][16 B]
+  static constexpr int STAGES = NQP <= 8 ? 3 : 2;
+  static constexpr int TCOLS = 2 * NS + 2 * NO;          // S0 S1 O0 O1
+  static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : 256;
+  static_assert(TCOLS <= 256, "two CTAs per SM share the 512 TMEM columns");
   static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
-  // shared memory plan (offsets from a 1024-aligned base)
+  // shared memory plan (offsets from the 1024-aligned dynamic shared memory base)
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + STAGES * kTileBytes;
-  static constexpr int VC_OFF = V_OFF + STAGES * kTileBytes;  // e2m3: converted V, two slots
-  static constexpr int Q_OFF = VC_OFF + ((FMT == MJ_KV_E2M3) ? 2 * kTileBytes : 0);  // two slots (jobs)
-  static constexpr int P_OFF = Q_OFF + 2 * QBYTES;                                  // two slots (tiles)
-  static constexpr int BAR_OFF = P_OFF + 2 * QBYTES;
+  static constexpr int Q_OFF = V_OFF + STAGES * kTileBytes;  // two slots (jobs)
+  static constexpr int P_OFF = (Q_OFF + 2 * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
+  static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;
   static constexpr int NBARS = 4 * STAGES + 2 * 8 + 1;  // k/v full/empty rings, 8 pairs, drain
   static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[2][4][NQP]
-  static constexpr int LIM_OFF = RED_OFF + 2 * 4 * NQP * 4;  // int lim[NQP]
-  static constexpr int MISC_OFF = LIM_OFF + NQP * 4;    // tmem base, abort flag, l scratch [4][NQP]
-  static constexpr int SMEM = MISC_OFF + 64 + 4 * 4 * NQP + 1024;  // + alignment slack
+  static constexpr int MISC_OFF = RED_OFF + 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [4][NQP]
+  static constexpr int SMEM = MISC_OFF + 64 + 4 * 4 * NQP;
 };
 
 struct Bars {
@@ -128,10 +133,9 @@ __device__ __forceinline__ void store_split(unsigned char* buf, int r, int t, ui
   buf[sw128_offset(2 * NQP + r + 1, t)] = (uint8_t)(lb >> 8);
 }
 
-// 3*NQP TMEM columns of this thread's lane -> v
-template <int NQP>
+// C TMEM columns (a multiple of 8) of this thread's lane -> v
+template <int C>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
-  constexpr int C = (3 * NQP) < 16 ? 16 : 3 * NQP;
 #pragma unroll
   for (int c = 0; c + 16 <= C; c += 16) tmem_ld16(taddr + c, v + c);
   if (C % 16) tmem_ld8(taddr + (C / 16) * 16, v + (C / 16) * 16);
@@ -153,11 +157,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     decode_tc_kernel(const __grid_constant__ mj_decode_args a, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
   using C = Cfg<FMT, NQP>;
-  constexpr int N = C::N;
+  constexpr int NS = C::NS, NO = C::NO;
   constexpr int S = C::STAGES;
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw;  // 1024-aligned: the 128-byte swizzle atoms need it
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (reinterpret_cast<uintptr_t>(sm) & 1023) {  // uniform: no barrier or TMEM touched yet
+    if (threadIdx.x == 0) flag(a.status, MJ_DEV_BAD_SPLIT);
+    return;
+  }
   const int h_k = a.h_k;
   const int total_jobs = a.num_work * h_k;  // job p: work item p / h_k, KV head p % h_k
 
@@ -177,19 +185,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   b.q_full = b.v_free + 2;
   b.drain = b.q_full + 2;
   float* red = reinterpret_cast<float*>(sm + C::RED_OFF);   // [2][4][NQP]
-  int* lim_s = reinterpret_cast<int*>(sm + C::LIM_OFF);      // [NQP]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::MISC_OFF + 4);
+  int& never_abort = *reinterpret_cast<int*>(sm + C::MISC_OFF + 8);  // no one sets it: drains wait on time only
   float* lred = reinterpret_cast<float*>(sm + C::MISC_OFF + 64);  // [4][NQP]
-  __shared__ int never_abort;  // a flag no one sets: drains wait on time only
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&b.k_full[i], 1);
       mbar_init(&b.k_empty[i], 1);
       mbar_init(&b.v_full[i], 1);
-      // e2m3: the converter warps release the raw V slot; e4m3: the PV MMA does
-      mbar_init(&b.v_empty[i], FMT == MJ_KV_E2M3 ? 64 : 1);
+      mbar_init(&b.v_empty[i], 1);  // released by the PV MMA
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b.s_full[i], 1);
@@ -217,13 +223,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S0 [0,N) S1 [N,2N) O0 [2N,3N) O1 [3N,4N)
+  const uint32_t tmem = *tmem_slot;  // S0 [0,NS) S1 [NS,2NS) O0 [2NS,2NS+NO) O1 [2NS+NO,2NS+2NO)
 
   auto kbuf = [&](int st) { return sm + C::K_OFF + st * kTileBytes; };
   auto vbuf = [&](int st) { return sm + C::V_OFF + st * kTileBytes; };
-  auto vcvt = [&](int i) { return sm + C::VC_OFF + i * kTileBytes; };
   auto qbuf = [&](int i) { return sm + C::Q_OFF + i * C::QBYTES; };
-  auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::QBYTES; };
+  auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::PBYTES; };
   auto give_up = [&]() {
     *abort_flag = 1;
     flag(a.status, MJ_DEV_TIMEOUT);
@@ -295,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else if (warp == kWarpMma) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc_s = idesc_f8f6f4(FMT == MJ_KV_E2M3 ? 3u : 0u, 0u, 0u, 0u, (uint32_t)N);
-      const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 0u, (uint32_t)N);
+      const uint32_t idesc_s = idesc_f8f6f4(FMT == MJ_KV_E2M3 ? 3u : 0u, 0u, 0u, 0u, (uint32_t)NS);
+      const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 1u, (uint32_t)NO);  // V and P both MN-major
       bool ok = true;
       int it = 0, jc = 0;
       // O_t^T = V_t^T . P_t^T for global tile t
@@ -307,15 +312,17 @@ __global__ void __launch_bounds__(kThreads, 2)
               mbar_wait(&b.o_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)))
           return false;
         tc_fence_after();
-        const uint32_t vaddr = smem_addr(FMT == MJ_KV_E2M3 ? vcvt(t & 1) : vbuf(st));
+        const uint32_t vaddr = smem_addr(vbuf(st));
         const uint32_t paddr = smem_addr(pbuf(t & 1));
-        const uint32_t d = tmem + (uint32_t)(2 * N + (t & 1) * N);
+        const uint32_t d = tmem + (uint32_t)(2 * NS + (t & 1) * NO);
+        // P^T is [128 s][16 B] per group of 16 rows: 8-row core matrices 128 B
+        // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_f8f6f4(d, smem_desc_sw128(vaddr + 4096 * k, kTileBytes, 1024), smem_desc_sw128(paddr + 32 * k, 16, 1024),
+          mma_f8f6f4(d, smem_desc_sw128(vaddr + 4096 * k, kTileBytes, 1024), smem_desc_noswz(paddr + 512 * k, 128, 2048),
                      idesc_o, k > 0);
         mma_commit(&b.o_full[t & 1]);
-        if (FMT != MJ_KV_E2M3) mma_commit(&b.v_empty[st]);
+        mma_commit(&b.v_empty[st]);
         mma_commit(&b.v_free[t & 1]);
         return true;
       };
@@ -333,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!ok) break;
           tc_fence_after();
           const uint32_t kaddr = smem_addr(kbuf(st));
-          const uint32_t d = tmem + (uint32_t)((it & 1) * N);
+          const uint32_t d = tmem + (uint32_t)((it & 1) * NS);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, 1024), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
@@ -365,12 +372,11 @@ __global__ void __launch_bounds__(kThreads, 2)
              mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
         if (!ok) break;
         if (FMT == MJ_KV_E2M3) {
-          const uint4* src = reinterpret_cast<const uint4*>(vbuf(st));
-          uint4* dst = reinterpret_cast<uint4*>(vcvt(it & 1));
+          // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot
+          uint4* v4 = reinterpret_cast<uint4*>(vbuf(st));
 #pragma unroll 4
-          for (int c = ct; c < kTileBytes / 16; c += 64) dst[c] = e2m3x16_to_e4m3(src[c]);
+          for (int c = ct; c < kTileBytes / 16; c += 64) v4[c] = e2m3x16_to_e4m3(v4[c]);
           // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
-          mbar_arrive(&b.v_empty[st]);  // raw V slot free for the next TMA
         } else {
           // e4m3 rows past the sequence end inside its last page may hold NaN
           // bytes; NaN * 0 would poison O, so zero them (their P is 0)
@@ -392,12 +398,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int wq = warp - kWarpSm0;             // TMEM lane quarter
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const int h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r;
-    // padding rows of the Q and P operands (past 3*NQP) stay zero for the whole kernel
+    // Q rows past 3*NQP (padding to the MMA's N) stay zero for the whole kernel
     for (int i = 0; i < 2; ++i)
-      for (int row = 3 * NQP; row < N; ++row) {
-        qbuf(i)[sw128_offset(row, t)] = 0;
-        pbuf(i)[sw128_offset(row, t)] = 0;
-      }
+      for (int row = 3 * NQP; row < NS; ++row) qbuf(i)[sw128_offset(row, t)] = 0;
     int it = 0, jc = 0;
     bool aborted = false;
     for (int p = blockIdx.x; !aborted && p < total_jobs; p += gridDim.x) {
@@ -406,23 +409,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int L = a.seq_lens[seq];
       // ---- Q of this job: head-dim element t of every query row, split in 3 e4m3 terms
       float qv[NQP];
+      int lim[NQP];  // last visible key of each query row (-1: padding row)
       float qmax = 0.f;
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
         float x = 0.f;
+        lim[r] = -1;
         if (r < n_q) {
           const int qi = r / h_r, rr = r % h_r;
           const int64_t tok = (int64_t)seq * q_len + qi;
           const int qh = h * h_r + rr;
           x = load_elem(a.q, tok * a.q_stride_tok + qh * a.q_stride_head + t, a.q_dtype);
           if (a.q_mul) x *= a.q_mul[(int64_t)qh * 128 + t];
+          lim[r] = a.causal ? L - q_len + qi : L - 1;
         }
         qv[r] = x;
         qmax = fmaxf(qmax, fabsf(x));
       }
       qmax = warp_max_f32(qmax);
       if (lane == 0) red[wq] = qmax;
-      if (t < NQP) lim_s[t] = (t < n_q) ? (a.causal ? L - q_len + t / h_r : L - 1) : -1;
       if (named_bar_or(1, 128, *abort_flag != 0)) break;
       qmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
       const float qs = qmax > 0.f ? 224.f / qmax : 1.f;  // |q * qs| <= 224
@@ -441,75 +446,112 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (t == 0) mbar_arrive(&b.q_full[jc & 1]);
       ++jc;
 
-      float m[NQP], l[NQP], cr[NQP], oacc[NQP];
+      // m: running max (log2 units) -- raised lazily, see kRescaleLog2;
+      // cr: correction of the current tile, crp: of the previous one
+      float m[NQP], l[NQP], cr[NQP], crp[NQP], oacc[NQP];
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
         m[r] = -INFINITY;
         l[r] = 0.f;
         cr[r] = 1.f;
+        crp[r] = 1.f;
         oacc[r] = 0.f;
       }
-      // fold the O tile of global tile tt into the register accumulator (uses cr of that tile)
+      // fold the O tile of global tile tt into the register accumulator; crp
+      // holds that tile's correction (accumulator max -> the tile's max)
       auto fold = [&](int tt) {
         if (!mbar_wait(&b.o_full[tt & 1], (tt >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
         tc_fence_after();
-        float ov[N];
-        tmem_ld_cols<NQP>(tmem + (uint32_t)(2 * N + (tt & 1) * N) + lane_base, ov);
+        float ov[NO];
+        tmem_ld_cols<NO>(tmem + (uint32_t)(2 * NS + (tt & 1) * NO) + lane_base, ov);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&b.o_free[tt & 1]);
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) oacc[r] = fmaf(oacc[r], cr[r], combine3<NQP>(ov, r));
+        for (int r = 0; r < NQP; ++r) oacc[r] = fmaf(oacc[r], crp[r], combine3<NQP>(ov, r));
       };
 
       const int n = te - tb;
+      // Per tile: S_i -> P_i first, then fold O of tile i-1, so the PV MMA of
+      // tile i runs while this warpgroup works on tile i+1.
       for (int i = 0; i < n; ++i, ++it) {
-        if (i >= 1) fold(it - 1);
         if (!mbar_wait(&b.s_full[it & 1], (it >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
         tc_fence_after();
-        float sv[N];
-        tmem_ld_cols<NQP>(tmem + (uint32_t)((it & 1) * N) + lane_base, sv);
+        float sv[NS];
+        tmem_ld_cols<NS>(tmem + (uint32_t)((it & 1) * NS) + lane_base, sv);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&b.s_free[it & 1]);
         const int j = (tb + i) * kTileRows + t;  // this thread's KV row
-        float* rd = red + (it & 1) * 4 * NQP;
+        bool grow = false;
 #pragma unroll
         for (int r = 0; r < NQP; ++r) {
           float s = combine3<NQP>(sv, r) * c2;
-          if (j > lim_s[r]) s = -INFINITY;
+          if (j > lim[r]) s = -INFINITY;
           sv[r] = s;
-          const float wm = warp_max_f32(s);
-          if (lane == 0) rd[wq * NQP + r] = wm;
+          grow = grow || (s > m[r] + kRescaleLog2);
         }
-        // the max exchange barrier doubles as a uniform abort vote
-        if (named_bar_or(1, 128, *abort_flag != 0)) {
-          aborted = true;
-          break;
+        // one barrier per tile: a uniform vote on "some score outgrew its row's
+        // max" (or abort); only then do the rows exchange their tile maxima
+        if (named_bar_or(1, 128, grow || *abort_flag != 0)) {
+          if (named_bar_or(1, 128, *abort_flag != 0)) {
+            aborted = true;
+            break;
+          }
+          float* rd = red + (it & 1) * 4 * NQP;
+#pragma unroll
+          for (int r = 0; r < NQP; ++r) {
+            const float wm = warp_max_f32(sv[r]);
+            if (lane == 0) rd[wq * NQP + r] = wm;
+          }
+          named_bar_sync(1, 128);
+#pragma unroll
+          for (int r = 0; r < NQP; ++r) {
+            const float mt = fmaxf(fmaxf(rd[r], rd[NQP + r]), fmaxf(rd[2 * NQP + r], rd[3 * NQP + r]));
+            if (mt > m[r]) {
+              const float corr = m[r] == -INFINITY ? 0.f : exp2_approx(m[r] - mt);
+              l[r] *= corr;
+              cr[r] = corr;
+              m[r] = mt;
+            } else {
+              cr[r] = 1.f;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < NQP; ++r) cr[r] = 1.f;
         }
-        unsigned char* pb = pbuf(it & 1);
+        // P: three e4m3 terms per row, this thread's KV row s = t packed as the
+        // 16-byte row s of each MN-major group (N rows hi | mid | lo | padding)
+        uint32_t w[NO / 4];
+#pragma unroll
+        for (int k = 0; k < NO / 4; ++k) w[k] = 0u;
 #pragma unroll
         for (int r = 0; r < NQP; r += 2) {
           float p2[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int rr = r + u;
-            const float mt = fmaxf(fmaxf(rd[rr], rd[NQP + rr]), fmaxf(rd[2 * NQP + rr], rd[3 * NQP + rr]));
-            const float m_new = fmaxf(m[rr], mt);
-            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            const float corr = exp2f(m[rr] - m_use);  // m = -inf -> 0
-            const float pv = exp2f(sv[rr] - m_use);   // masked -> 0
-            l[rr] = fmaf(l[rr], corr, pv);
-            m[rr] = m_new;
-            cr[rr] = corr;
+            const float pv = m[rr] == -INFINITY ? 0.f : exp2_approx(sv[rr] - m[rr]);  // masked -> 0
+            l[rr] += pv;
             p2[u] = pv * kPScale;
           }
           uint16_t hb, mb, lb;
           split3(p2[0], p2[1], hb, mb, lb);
-          store_split<NQP>(pb, r, t, hb, mb, lb);
+          const int sh = 16 * ((r >> 1) & 1);
+          w[r >> 2] |= (uint32_t)hb << sh;
+          w[(NQP + r) >> 2] |= (uint32_t)mb << sh;
+          w[(2 * NQP + r) >> 2] |= (uint32_t)lb << sh;
         }
+        unsigned char* pb = pbuf(it & 1);
+#pragma unroll
+        for (int g = 0; g < NO / 16; ++g)
+          *reinterpret_cast<uint4*>(pb + g * 2048 + t * 16) = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
         fence_proxy_async_smem();
         mbar_arrive(&b.p_full[it & 1]);
+        if (i >= 1) fold(it - 1);
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) crp[r] = cr[r];
       }
       if (aborted) break;
       fold(it - 1);

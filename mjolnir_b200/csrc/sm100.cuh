@@ -181,6 +181,24 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// Shared-memory matrix descriptor without swizzle (canonical "interleaved"
+// layout of 8-row x 16-byte core matrices), sm_100 version 1.
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version; layout type 0 = no swizzle
+  return d;
+}
+
+// 2^x for x <= 0 (hardware approximation, flushes subnormal results to 0).
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Byte offset of element (row, k) of a [rows][128 B] tile in the 128-byte
 // swizzled layout (16-byte chunk index XOR row % 8), tile base 1024-aligned.
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t kbyte) {
