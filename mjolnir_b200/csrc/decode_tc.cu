@@ -63,6 +63,7 @@ constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpCvt0 = 2;   // warps 2-3: V conversion (e2m3) / tail zeroing (e4m3)
 constexpr int kWarpSm0 = 4;    // warps 4-7: softmax warpgroup
+constexpr int kCvtThreads = 64 + 128;  // threads that share an e2m3 V tile conversion
 
 template <int FMT, int NQP>
 struct Cfg {
@@ -152,7 +153,11 @@ __device__ __forceinline__ float combine3(const float* v, int r) {
 namespace mj {
 namespace tc {
 
-template <int FMT, int NQP>
+// FUSED: K and V of a page arrive in one TMA box (the vLLM / reference layout
+// (pages, h_k, page_size, K row | V row)); the box lands as alternating 1 KB
+// K and V swizzle atoms, so both operands see an atom stride of 2048 B.
+// Otherwise K and V are separate boxes into separate tiles (atom stride 1024 B).
+template <int FMT, int NQP, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 2)
     decode_tc_kernel(const __grid_constant__ mj_decode_args a, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
@@ -203,7 +208,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&b.p_full[i], 128);
       mbar_init(&b.o_full[i], 1);
       mbar_init(&b.o_free[i], 128);
-      mbar_init(&b.v_ready[i], 64);
+      // e2m3: converter warps and softmax warpgroup share the V conversion
+      mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? 64 + 128 : 64);
       mbar_init(&b.v_free[i], 1);
       mbar_init(&b.q_full[i], 1);
     }
@@ -225,8 +231,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;  // S0 [0,NS) S1 [NS,2NS) O0 [2NS,2NS+NO) O1 [2NS+NO,2NS+2NO)
 
-  auto kbuf = [&](int st) { return sm + C::K_OFF + st * kTileBytes; };
-  auto vbuf = [&](int st) { return sm + C::V_OFF + st * kTileBytes; };
+  constexpr uint32_t ATOM = FUSED ? 2048u : 1024u;  // byte stride between 8-row swizzle atoms of K (or V)
+  auto kbuf = [&](int st) { return FUSED ? sm + st * 2 * kTileBytes : sm + C::K_OFF + st * kTileBytes; };
+  auto vbuf = [&](int st) { return FUSED ? sm + st * 2 * kTileBytes + 1024 : sm + C::V_OFF + st * kTileBytes; };
+  // byte offset of 16-byte chunk c (row c / 8) of the V tile, and of row r
+  auto vchunk = [&](int c) { return (uint32_t)((c >> 6) * ATOM + (c & 63) * 16); };
   auto qbuf = [&](int i) { return sm + C::Q_OFF + i * C::QBYTES; };
   auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::PBYTES; };
   auto give_up = [&]() {
@@ -271,6 +280,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t par = ((it / S) & 1) ^ 1;
         const int pg = pg_next;
         if (tile + 1 < te) pg_next = page_coord(tile + 1);
+        if (FUSED) {  // one box per page: K and V rows together (the stage frees after PV)
+          if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * C::K_TX);
+          __syncwarp();
+          if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h);
+          k_issued = it + 1;
+          continue;
+        }
         if (lane == 0) ok = mbar_wait(&b.k_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
@@ -319,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_f8f6f4(d, smem_desc_sw128(vaddr + 4096 * k, kTileBytes, 1024), smem_desc_noswz(paddr + 512 * k, 128, 2048),
+          mma_f8f6f4(d, smem_desc_sw128(vaddr + 4 * ATOM * k, kTileBytes, ATOM), smem_desc_noswz(paddr + 512 * k, 128, 2048),
                      idesc_o, k > 0);
         mma_commit(&b.o_full[t & 1]);
         mma_commit(&b.v_empty[st]);
@@ -343,10 +362,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint32_t d = tmem + (uint32_t)((it & 1) * NS);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, 1024), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
+            mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
                        idesc_s, k > 0);
           mma_commit(&b.s_full[it & 1]);
-          mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
+          if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
           if (i >= 1) ok = pv(it - 1);
         }
         if (ok) ok = pv(it - 1);  // the job's last tile
@@ -368,14 +387,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int tile = tb; tile < te; ++tile, ++it) {
         const int st = it % S;
         // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
-        ok = mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+        ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
              mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
         if (!ok) break;
         if (FMT == MJ_KV_E2M3) {
-          // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot
-          uint4* v4 = reinterpret_cast<uint4*>(vbuf(st));
-#pragma unroll 4
-          for (int c = ct; c < kTileBytes / 16; c += 64) v4[c] = e2m3x16_to_e4m3(v4[c]);
+          // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
+          // this role converts chunks ct, ct + kCvtThreads, ...; the softmax
+          // warpgroup converts the others after publishing P
+          unsigned char* vb = vbuf(st);
+#pragma unroll 2
+          for (int c = ct; c < kTileBytes / 16; c += kCvtThreads) {
+            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+            *q = e2m3x16_to_e4m3(*q);
+          }
           // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
         } else {
           // e4m3 rows past the sequence end inside its last page may hold NaN
@@ -383,8 +407,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int valid = L - tile * kTileRows;
           if (valid < kTileRows) {
             const int r0 = valid > 0 ? valid : 0;
-            uint4* v4 = reinterpret_cast<uint4*>(vbuf(st));
-            for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64) v4[c] = make_uint4(0, 0, 0, 0);
+            unsigned char* vb = vbuf(st);
+            for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64)
+              *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
           }
         }
         fence_proxy_async_smem();
@@ -549,6 +574,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           *reinterpret_cast<uint4*>(pb + g * 2048 + t * 16) = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
         fence_proxy_async_smem();
         mbar_arrive(&b.p_full[it & 1]);
+        if (FMT == MJ_KV_E2M3) {  // this warpgroup's share of the V conversion
+          const int st = it % S;
+          if (!FUSED && !mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
+          unsigned char* vb = vbuf(st);
+#pragma unroll 2
+          for (int c = 64 + t; c < kTileBytes / 16; c += kCvtThreads) {
+            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+            *q = e2m3x16_to_e4m3(*q);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&b.v_ready[it & 1]);
+        }
         if (i >= 1) fold(it - 1);
 #pragma unroll
         for (int r = 0; r < NQP; ++r) crp[r] = cr[r];
@@ -669,17 +706,52 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t s_page, int64_t s
 // Persistent launch: one CTA per resident slot (SMs x CTAs per SM), each walking
 // the job list (work item, KV head) with a stride of the grid size. The work
 // list is longest-first, so the round-robin is a longest-first assignment.
-template <int FMT, int NQP>
+// K and V rows of a page interleaved in one block per (page, KV head): the
+// vLLM / reference layout (pages, h_k, page_size, K row | V row). Then one
+// 5-D box -- (codes, 8 rows, K|V, row groups, page * h_k + head) -- loads a
+// page's K and V at once: half the TMA operations of separate boxes.
+static bool fused_layout(const mj_decode_args& a, int64_t* pagehead_stride) {
+  const int64_t rb = a.kv_format == MJ_KV_E2M3 ? 96 : 128;
+  if ((uintptr_t)a.v_cache != (uintptr_t)a.k_cache + (uintptr_t)rb) return false;
+  if (a.k_stride_page != a.v_stride_page || a.k_stride_row != a.v_stride_row || a.k_stride_head != a.v_stride_head)
+    return false;
+  if (a.page_size % 8 || a.k_stride_row < 2 * rb) return false;
+  if (a.h_k > 1) {
+    if (a.k_stride_page != (int64_t)a.h_k * a.k_stride_head) return false;
+    *pagehead_stride = a.k_stride_head;
+  } else {
+    *pagehead_stride = a.k_stride_page ? a.k_stride_page : (int64_t)a.page_size * a.k_stride_row;
+  }
+  return *pagehead_stride >= (int64_t)a.page_size * a.k_stride_row;
+}
+
+static bool make_map_fused(CUtensorMap* m, const mj_decode_args& a, int64_t pagehead_stride) {
+  const bool e2m3 = a.kv_format == MJ_KV_E2M3;
+  const int64_t rb = e2m3 ? 96 : 128;
+  const int64_t heads = a.h_k > 1 ? a.h_k : 1;
+  cuuint64_t dims[5] = {128, 8, 2, (cuuint64_t)(a.page_size / 8), (cuuint64_t)(a.num_pages * heads)};
+  cuuint64_t strides[4] = {(cuuint64_t)a.k_stride_row, (cuuint64_t)rb, (cuuint64_t)(8 * a.k_stride_row),
+                           (cuuint64_t)pagehead_stride};
+  cuuint32_t box[5] = {128, 8, 2, (cuuint32_t)(a.page_size / 8), 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode_fn()(m, e2m3 ? CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 5,
+                           const_cast<void*>(a.k_cache), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int FMT, int NQP, bool FUSED>
 static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream) {
   const int smem = tc::Cfg<FMT, NQP>::SMEM;
   static int slots = 0;  // resident CTAs on this device (set once: one process per GPU)
   if (!slots) {
-    cudaError_t e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     // without a carveout preference the occupancy is computed for a smaller
     // shared-memory partition and one CTA per SM would be assumed
-    e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP, FUSED>, cudaFuncAttributePreferredSharedMemoryCarveout,
                              (int)cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     // resident CTAs per SM from the device limits: shared memory (with the
@@ -691,7 +763,7 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
     if ((e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&reserve, cudaDevAttrReservedSharedMemoryPerBlock, dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev)) != cudaSuccess) return e;
-    if ((e = cudaFuncGetAttributes(&fa, tc::decode_tc_kernel<FMT, NQP>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&fa, tc::decode_tc_kernel<FMT, NQP, FUSED>)) != cudaSuccess) return e;
     int occ = smem_sm / (smem + (int)fa.sharedSizeBytes + reserve);
     const int regs_cta = ((fa.numRegs + 7) / 8) * 8 * tc::kThreads;
     occ = occ < regs_sm / regs_cta ? occ : regs_sm / regs_cta;
@@ -701,8 +773,21 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
   }
   const int64_t jobs = (int64_t)a.num_work * a.h_k;
   const unsigned grid = (unsigned)(jobs < slots ? jobs : slots);
-  tc::decode_tc_kernel<FMT, NQP><<<grid, tc::kThreads, smem, stream>>>(a, mk, mv);
+  tc::decode_tc_kernel<FMT, NQP, FUSED><<<grid, tc::kThreads, smem, stream>>>(a, mk, mv);
   return cudaGetLastError();
+}
+
+template <bool FUSED>
+static cudaError_t dispatch_nq(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
+                               cudaStream_t stream) {
+  if (a.kv_format == MJ_KV_E2M3) {
+    if (n_q <= 4) return launch_tc_t<MJ_KV_E2M3, 4, FUSED>(a, mk, mv, stream);
+    return n_q <= 8 ? launch_tc_t<MJ_KV_E2M3, 8, FUSED>(a, mk, mv, stream)
+                    : launch_tc_t<MJ_KV_E2M3, 16, FUSED>(a, mk, mv, stream);
+  }
+  if (n_q <= 4) return launch_tc_t<MJ_KV_FP8_E4M3, 4, FUSED>(a, mk, mv, stream);
+  return n_q <= 8 ? launch_tc_t<MJ_KV_FP8_E4M3, 8, FUSED>(a, mk, mv, stream)
+                  : launch_tc_t<MJ_KV_FP8_E4M3, 16, FUSED>(a, mk, mv, stream);
 }
 
 // Launch the tensor-core decode when it can run these arguments; *handled
@@ -711,17 +796,19 @@ cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool*
   *handled = false;
   if (tc_ineligible(a)) return cudaSuccess;
   CUtensorMap mk, mv;
-  if (!make_map(&mk, a.k_cache, a.k_stride_page, a.k_stride_row, a.k_stride_head, a) ||
-      !make_map(&mv, a.v_cache, a.v_stride_page, a.v_stride_row, a.v_stride_head, a))
+  int64_t ph_stride = 0;
+  const bool fused = fused_layout(a, &ph_stride);
+  if (fused) {
+    if (!make_map_fused(&mk, a, ph_stride)) return cudaErrorInvalidValue;
+    mv = mk;  // unused
+  } else if (!make_map(&mk, a.k_cache, a.k_stride_page, a.k_stride_row, a.k_stride_head, a) ||
+             !make_map(&mv, a.v_cache, a.v_stride_page, a.v_stride_row, a.v_stride_head, a)) {
     return cudaErrorInvalidValue;
+  }
   *handled = true;
   const int n_q = a.q_len * (a.h_q / a.h_k);
-  if (a.kv_format == MJ_KV_E2M3) {
-    if (n_q <= 4) return launch_tc_t<MJ_KV_E2M3, 4>(a, mk, mv, stream);
-    return n_q <= 8 ? launch_tc_t<MJ_KV_E2M3, 8>(a, mk, mv, stream) : launch_tc_t<MJ_KV_E2M3, 16>(a, mk, mv, stream);
-  }
-  if (n_q <= 4) return launch_tc_t<MJ_KV_FP8_E4M3, 4>(a, mk, mv, stream);
-  return n_q <= 8 ? launch_tc_t<MJ_KV_FP8_E4M3, 8>(a, mk, mv, stream) : launch_tc_t<MJ_KV_FP8_E4M3, 16>(a, mk, mv, stream);
+  if (fused) return dispatch_nq<true>(a, n_q, mk, mv, stream);
+  return dispatch_nq<false>(a, n_q, mk, mv, stream);
 }
 
 }  // namespace mj
