@@ -34,6 +34,7 @@
 // Every mbarrier wait is bounded (MJ_TC_WAIT_NS); on a timeout the CTA sets
 // MJ_DEV_TIMEOUT in the status word, all roles stop at their next wait, wait
 // (bounded) for their in-flight copies and MMAs, free TMEM and return.
+#include <limits.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -145,6 +146,24 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
 template <int NQP>
 __device__ __forceinline__ float combine3(const float* v, int r) {
   return v[r] + v[NQP + r] * 0.0625f + v[2 * NQP + r] * 0.00390625f;
+}
+
+// rows r, r+1 of the three row blocks: hi + mid / 16 + lo / 256
+template <int NQP>
+__device__ __forceinline__ float2 combine3x2(const float* v, int r) {
+  const float2 hi = make_float2(v[r], v[r + 1]), mid = make_float2(v[NQP + r], v[NQP + r + 1]),
+               lo = make_float2(v[2 * NQP + r], v[2 * NQP + r + 1]);
+  return ffma2(lo, make_float2(0.00390625f, 0.00390625f), ffma2(mid, make_float2(0.0625f, 0.0625f), hi));
+}
+
+// split3 on a pair with packed residual arithmetic (the residuals are exact)
+__device__ __forceinline__ void split3x2(float2 y, uint16_t& hb, uint16_t& mb, uint16_t& lb) {
+  const float2 m16 = make_float2(-16.f, -16.f), p16 = make_float2(16.f, 16.f);
+  hb = f2_to_e4m3x2(y.x, y.y);
+  const float2 r1 = ffma2(e4m3x2_to_f2(hb), m16, fmul2(y, p16));
+  mb = f2_to_e4m3x2(r1.x, r1.y);
+  const float2 r2 = ffma2(e4m3x2_to_f2(mb), m16, fmul2(r1, p16));
+  lb = f2_to_e4m3x2(r2.x, r2.y);
 }
 
 }  // namespace tc
@@ -471,17 +490,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (t == 0) mbar_arrive(&b.q_full[jc & 1]);
       ++jc;
 
-      // m: running max (log2 units) -- raised lazily, see kRescaleLog2;
-      // cr: correction of the current tile, crp: of the previous one
-      float m[NQP], l[NQP], cr[NQP], crp[NQP], oacc[NQP];
+      // Query rows in pairs (packed f32x2 math). m: running max in log2 units,
+      // raised lazily (see kRescaleLog2); mu: the max the exponent uses (0
+      // while a row has seen no key); cr / crp: corrections of the current /
+      // previous tile; l: this thread's partial row sums; oa: O accumulator.
+      constexpr int NP = NQP / 2;
+      float2 m2[NP], mu2[NP], l2[NP], cr2[NP], crp2[NP], oa2[NP];
 #pragma unroll
-      for (int r = 0; r < NQP; ++r) {
-        m[r] = -INFINITY;
-        l[r] = 0.f;
-        cr[r] = 1.f;
-        crp[r] = 1.f;
-        oacc[r] = 0.f;
+      for (int q = 0; q < NP; ++q) {
+        m2[q] = make_float2(-INFINITY, -INFINITY);
+        mu2[q] = make_float2(0.f, 0.f);
+        l2[q] = make_float2(0.f, 0.f);
+        cr2[q] = make_float2(1.f, 1.f);
+        crp2[q] = cr2[q];
+        oa2[q] = l2[q];
       }
+      int lim_min = INT_MAX;  // a tile ending at or before lim_min needs no causal mask
+#pragma unroll
+      for (int r = 0; r < NQP; ++r)
+        if (r < n_q) lim_min = min(lim_min, lim[r]);
+      const float2 c2v = make_float2(c2, c2);
       // fold the O tile of global tile tt into the register accumulator; crp
       // holds that tile's correction (accumulator max -> the tile's max)
       auto fold = [&](int tt) {
@@ -493,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_before();
         mbar_arrive(&b.o_free[tt & 1]);
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) oacc[r] = fmaf(oacc[r], crp[r], combine3<NQP>(ov, r));
+        for (int q = 0; q < NP; ++q) oa2[q] = ffma2(oa2[q], crp2[q], combine3x2<NQP>(ov, 2 * q));
       };
 
       const int n = te - tb;
@@ -507,14 +535,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&b.s_free[it & 1]);
-        const int j = (tb + i) * kTileRows + t;  // this thread's KV row
+        const int j0 = (tb + i) * kTileRows, j = j0 + t;  // this thread's KV row
+        const bool edge = j0 + kTileRows - 1 > lim_min;  // some row sees only part of this tile
+        float2 x2[NP];
         bool grow = false;
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) {
-          float s = combine3<NQP>(sv, r) * c2;
-          if (j > lim[r]) s = -INFINITY;
-          sv[r] = s;
-          grow = grow || (s > m[r] + kRescaleLog2);
+        for (int q = 0; q < NP; ++q) {
+          float2 v = fmul2(combine3x2<NQP>(sv, 2 * q), c2v);
+          if (edge) {
+            if (j > lim[2 * q]) v.x = -INFINITY;
+            if (j > lim[2 * q + 1]) v.y = -INFINITY;
+          }
+          x2[q] = v;
+          grow = grow || (v.x > m2[q].x + kRescaleLog2) || (v.y > m2[q].y + kRescaleLog2);
         }
         // one barrier per tile: a uniform vote on "some score outgrew its row's
         // max" (or abort); only then do the rows exchange their tile maxima
@@ -525,45 +558,48 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           float* rd = red + (it & 1) * 4 * NQP;
 #pragma unroll
-          for (int r = 0; r < NQP; ++r) {
-            const float wm = warp_max_f32(sv[r]);
-            if (lane == 0) rd[wq * NQP + r] = wm;
+          for (int q = 0; q < NP; ++q) {
+            const float w0 = warp_max_f32(x2[q].x), w1 = warp_max_f32(x2[q].y);
+            if (lane == 0) {
+              rd[wq * NQP + 2 * q] = w0;
+              rd[wq * NQP + 2 * q + 1] = w1;
+            }
           }
           named_bar_sync(1, 128);
 #pragma unroll
           for (int r = 0; r < NQP; ++r) {
             const float mt = fmaxf(fmaxf(rd[r], rd[NQP + r]), fmaxf(rd[2 * NQP + r], rd[3 * NQP + r]));
-            if (mt > m[r]) {
-              const float corr = m[r] == -INFINITY ? 0.f : exp2_approx(m[r] - mt);
-              l[r] *= corr;
-              cr[r] = corr;
-              m[r] = mt;
+            float& mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
+            float& ur = (r & 1) ? mu2[r >> 1].y : mu2[r >> 1].x;
+            float& lr = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
+            float& cc = (r & 1) ? cr2[r >> 1].y : cr2[r >> 1].x;
+            if (mt > mr) {
+              cc = mr == -INFINITY ? 0.f : exp2_approx(mr - mt);
+              lr *= cc;
+              mr = mt;
+              ur = mt;
             } else {
-              cr[r] = 1.f;
+              cc = 1.f;
             }
           }
         } else {
 #pragma unroll
-          for (int r = 0; r < NQP; ++r) cr[r] = 1.f;
+          for (int q = 0; q < NP; ++q) cr2[q] = make_float2(1.f, 1.f);
         }
         // P: three e4m3 terms per row, this thread's KV row s = t packed as the
         // 16-byte row s of each MN-major group (N rows hi | mid | lo | padding)
         uint32_t w[NO / 4];
 #pragma unroll
         for (int k = 0; k < NO / 4; ++k) w[k] = 0u;
+        const float2 ps2 = make_float2(kPScale, kPScale);
 #pragma unroll
-        for (int r = 0; r < NQP; r += 2) {
-          float p2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int rr = r + u;
-            const float pv = m[rr] == -INFINITY ? 0.f : exp2_approx(sv[rr] - m[rr]);  // masked -> 0
-            l[rr] += pv;
-            p2[u] = pv * kPScale;
-          }
+        for (int q = 0; q < NP; ++q) {
+          const float2 d = fadd2(x2[q], make_float2(-mu2[q].x, -mu2[q].y));
+          const float2 pv = make_float2(exp2_approx(d.x), exp2_approx(d.y));  // masked -> 0
+          l2[q] = fadd2(l2[q], pv);
           uint16_t hb, mb, lb;
-          split3(p2[0], p2[1], hb, mb, lb);
-          const int sh = 16 * ((r >> 1) & 1);
+          split3x2(fmul2(pv, ps2), hb, mb, lb);
+          const int r = 2 * q, sh = 16 * (q & 1);
           w[r >> 2] |= (uint32_t)hb << sh;
           w[(NQP + r) >> 2] |= (uint32_t)mb << sh;
           w[(2 * NQP + r) >> 2] |= (uint32_t)lb << sh;
@@ -588,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (i >= 1) fold(it - 1);
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) crp[r] = cr[r];
+        for (int q = 0; q < NP; ++q) crp2[q] = cr2[q];
       }
       if (aborted) break;
       fold(it - 1);
@@ -596,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // ---- epilogue: l per query row (sum of the per-thread partials), outputs
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
-        float x = l[r];
+        float x = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
         if (lane == 0) lred[wq * NQP + r] = x;
@@ -618,8 +654,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int qi = r / h_r, rr = r % h_r;
             const int64_t tok = (int64_t)seq * q_len + qi;
             const int qh = h * h_r + rr;
-            float o = oacc[r] * inv;
-            const float lse = lt > 0.f ? (m[r] + log2f(lt)) * kLn2 : -INFINITY;
+            float o = ((r & 1) ? oa2[r >> 1].y : oa2[r >> 1].x) * inv;
+            const float mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
+            const float lse = lt > 0.f ? (mr + log2f(lt)) * kLn2 : -INFINITY;
             if (final_out) {
               if (a.o_mul) o *= a.o_mul[(int64_t)qh * 128 + t];
               store_elem(a.o, tok * a.o_stride_tok + qh * a.o_stride_head + t, a.o_dtype, o);
