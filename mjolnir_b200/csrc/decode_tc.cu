@@ -191,7 +191,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
   const int h_k = a.h_k;
-  const int total_jobs = a.num_work * h_k;  // job p: work item p / h_k, KV head p % h_k
+  // A job is (work item, KV head, row group): a CTA serves at most NQP query
+  // rows; a larger GQA x draft group is cut into n_rg row groups whose jobs
+  // are adjacent in the list, so CTAs reading the same KV stream run side by
+  // side and the repeat reads hit L2.
+  const int n_q_all = a.q_len * (a.h_q / h_k);
+  const int n_rg = (n_q_all + NQP - 1) / NQP;
+  const int total_jobs = a.num_work * h_k * n_rg;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
   Bars b;
@@ -262,7 +268,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     flag(a.status, MJ_DEV_TIMEOUT);
   };
   // every role walks the same job list and skips the same empty items
-  auto job = [&](int p, int& seq, int& tb, int& te, int& split, int& h) {
+  auto job = [&](int p, int& seq, int& tb, int& te, int& split, int& h, int& g) {
+    g = p % n_rg;
+    p /= n_rg;
     const int4 wi = reinterpret_cast<const int4*>(a.work)[p / h_k];
     seq = wi.x;
     tb = wi.y;
@@ -279,8 +287,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     int it = 0, k_issued = 0, v_issued = 0;
     bool ok = true;
     for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
-      int seq, tb, te, split, h;
-      if (!job(p, seq, tb, te, split, h)) continue;
+      int seq, tb, te, split, h, g;
+      if (!job(p, seq, tb, te, split, h, g)) continue;
       const int L = a.seq_lens[seq];
       const int32_t* bt = a.block_table + (int64_t)seq * a.block_table_stride;
       auto page_coord = [&](int tile) {
@@ -365,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         return true;
       };
       for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
-        int seq, tb, te, split, h;
-        if (!job(p, seq, tb, te, split, h)) continue;
+        int seq, tb, te, split, h, g;
+        if (!job(p, seq, tb, te, split, h, g)) continue;
         ok = mbar_wait(&b.q_full[jc & 1], (jc >> 1) & 1, abort_flag, MJ_TC_WAIT_NS);
         const uint32_t qaddr = smem_addr(qbuf(jc & 1));
         ++jc;
@@ -400,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     int it = 0;
     bool ok = true;
     for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
-      int seq, tb, te, split, h;
-      if (!job(p, seq, tb, te, split, h)) continue;
+      int seq, tb, te, split, h, g;
+      if (!job(p, seq, tb, te, split, h, g)) continue;
       const int L = a.seq_lens[seq];
       for (int tile = tb; tile < te; ++tile, ++it) {
         const int st = it % S;
@@ -441,17 +449,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int t = threadIdx.x - kWarpSm0 * 32;  // 0..127: TMEM lane = KV row of a tile = head-dim index
     const int wq = warp - kWarpSm0;             // TMEM lane quarter
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
-    const int h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r;
+    const int h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r;  // rows of the whole group
     // Q rows past 3*NQP (padding to the MMA's N) stay zero for the whole kernel
     for (int i = 0; i < 2; ++i)
       for (int row = 3 * NQP; row < NS; ++row) qbuf(i)[sw128_offset(row, t)] = 0;
     int it = 0, jc = 0;
     bool aborted = false;
     for (int p = blockIdx.x; !aborted && p < total_jobs; p += gridDim.x) {
-      int seq, tb, te, split, h;
-      if (!job(p, seq, tb, te, split, h)) continue;
+      int seq, tb, te, split, h, g;
+      if (!job(p, seq, tb, te, split, h, g)) continue;
       const int L = a.seq_lens[seq];
-      // ---- Q of this job: head-dim element t of every query row, split in 3 e4m3 terms
+      // ---- Q of this job: head-dim element t of each of its query rows
+      // (group rows g*NQP + r), split in 3 e4m3 terms
+      const int row0 = g * NQP;
       float qv[NQP];
       int lim[NQP];  // last visible key of each query row (-1: padding row)
       float qmax = 0.f;
@@ -459,8 +469,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int r = 0; r < NQP; ++r) {
         float x = 0.f;
         lim[r] = -1;
-        if (r < n_q) {
-          const int qi = r / h_r, rr = r % h_r;
+        if (row0 + r < n_q) {
+          const int qi = (row0 + r) / h_r, rr = (row0 + r) % h_r;
           const int64_t tok = (int64_t)seq * q_len + qi;
           const int qh = h * h_r + rr;
           x = load_elem(a.q, tok * a.q_stride_tok + qh * a.q_stride_head + t, a.q_dtype);
@@ -508,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       int lim_min = INT_MAX;  // a tile ending at or before lim_min needs no causal mask
 #pragma unroll
       for (int r = 0; r < NQP; ++r)
-        if (r < n_q) lim_min = min(lim_min, lim[r]);
+        if (row0 + r < n_q) lim_min = min(lim_min, lim[r]);
       const float2 c2v = make_float2(c2, c2);
       // fold the O tile of global tile tt into the register accumulator; crp
       // holds that tile's correction (accumulator max -> the tile's max)
@@ -648,10 +658,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else {
 #pragma unroll
         for (int r = 0; r < NQP; ++r) {
-          if (r < n_q) {
+          if (row0 + r < n_q) {
+            const int R = row0 + r;  // row of the whole group
             const float lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
             const float inv = lt > 0.f ? vscale / lt : 0.f;
-            const int qi = r / h_r, rr = r % h_r;
+            const int qi = R / h_r, rr = R % h_r;
             const int64_t tok = (int64_t)seq * q_len + qi;
             const int qh = h * h_r + rr;
             float o = ((r & 1) ? oa2[r >> 1].y : oa2[r >> 1].x) * inv;
@@ -662,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               store_elem(a.o, tok * a.o_stride_tok + qh * a.o_stride_head + t, a.o_dtype, o);
               if (t == 0 && a.lse) a.lse[tok * a.h_q + qh] = lse;
             } else {
-              const int64_t row = (((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + r;
+              const int64_t row = (((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + R;
               a.o_part[row * 128 + t] = o;
               if (t == 0) a.lse_part[row] = lse;
             }
@@ -710,7 +721,6 @@ static EncodeTiledFn encode_fn() {
 const char* tc_ineligible(const mj_decode_args& a) {
   const int n_q = a.q_len * (a.h_q / a.h_k);
   if (a.head_size != 128) return "head_size != 128";
-  if (n_q > 16) return "more than 16 query rows per KV head";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";
   const uintptr_t al = a.kv_format == MJ_KV_E2M3 ? 32 : 16;
@@ -808,7 +818,8 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
     occ = occ < 2 ? occ : 2;  // __launch_bounds__ min blocks
     slots = sms * (occ > 0 ? occ : 1);
   }
-  const int64_t jobs = (int64_t)a.num_work * a.h_k;
+  const int n_q = a.q_len * (a.h_q / a.h_k);
+  const int64_t jobs = (int64_t)a.num_work * a.h_k * ((n_q + NQP - 1) / NQP);
   const unsigned grid = (unsigned)(jobs < slots ? jobs : slots);
   tc::decode_tc_kernel<FMT, NQP, FUSED><<<grid, tc::kThreads, smem, stream>>>(a, mk, mv);
   return cudaGetLastError();

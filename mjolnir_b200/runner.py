@@ -253,7 +253,10 @@ class DecodeRunner:
 
     # ------------------------------------------------------------------ plan
     def n_tiles(self, q_len: int) -> int:
-        return 1  # one CTA serves all q_len * h_r query rows of a KV head
+        """CTA jobs per (work item, KV head): the tensor-core kernel serves up to
+        16 query rows per job and cuts larger GQA x draft groups into row groups."""
+        n_q = q_len * self.h_r
+        return 1 if n_q <= 16 else -(-n_q // 16)
 
     def slots(self, q_len: int) -> int:
         return max(1, (self.sm_count * self.ctas_per_sm) // (self.h_k * self.n_tiles(q_len)))

@@ -92,7 +92,8 @@ def test_config1_shape(kernel):
 
 @pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
 @pytest.mark.parametrize("q_len,causal,h_q,kernel", [(4, True, 16, "simt"), (6, True, 16, "simt"), (3, False, 16, "simt"),
-                                                     (4, True, 8, "tc"), (2, False, 16, "tc"), (3, True, 8, "tc")])
+                                                     (4, True, 8, "tc"), (2, False, 16, "tc"), (3, True, 8, "tc"),
+                                                     (6, True, 16, "tc"), (4, True, 16, "tc"), (3, False, 16, "tc")])
 def test_mtp_rows(kv_format, q_len, causal, h_q, kernel):
     c = Case(seq_lens=(q_len, 700, 1500, 33), q_len=q_len, h_q=h_q, h_k=2, kv_format=kv_format, seed=5,
              descale="head" if kv_format == "fp8" else "tensor", layout="BHN2D")
@@ -112,6 +113,16 @@ def test_split_and_unsplit_agree(sm_count, kernel):
     ref, _ = c.oracle()
     T = c.b
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"sm {sm_count}")
+
+
+def test_tc_config4_shape_row_groups():
+    """BASELINE config 4 shape (64 q / 8 KV heads, q_len 6 causal: 48 rows per KV
+    head in 3 row groups), e2m3, shortened context."""
+    c = Case(seq_lens=(3000, 6, 1290), q_len=6, h_q=64, h_k=8, kv_format="e2m3", layout="BHN2D", seed=41)
+    out, _, _ = c.run(kernel="tc")
+    ref, _ = c.oracle()
+    T = c.b * 6
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what="config4 shape")
 
 
 def test_descale_per_seq_head_and_d256():
