@@ -171,6 +171,38 @@ int mj_decode_kernel(const mj_decode_args* args);
 /* LSE merge of the partials of every sequence with n_splits > 1 into O / LSE. */
 int mj_combine(const mj_decode_args* args, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* e2m3 -> e4m3 page expansion for steps a stock fallback backend runs on an */
+/* e2m3 cache. Replaces kvfp6.py:257-335 `expand_pages_to_fp8` (called from  */
+/* backend.py:573-607 on the page map of builder.py:479-509). Output page j  */
+/* (0 <= j < num_out_pages) receives the K and V rows of cache page          */
+/* src_pages[j]: each e4m3 byte = e4m3(code_value * ratio) with the fp32      */
+/* product rounded to nearest even and saturated at +-448 (ratio = 1 when    */
+/* the pointer is null, which gives the e2m3 values exactly). A src page     */
+/* outside [0, num_pages) flags MJ_DEV_BAD_PAGE and its output page is left  */
+/* untouched. Alignment: packed rows 4-byte aligned, output rows 16-byte.    */
+typedef struct mj_expand_args {
+  const void* k_cache;          /* e2m3 logical (num_pages, page_size, h_k, row_bytes) */
+  const void* v_cache;
+  int64_t k_stride_page, k_stride_row, k_stride_head; /* bytes */
+  int64_t v_stride_page, v_stride_row, v_stride_head; /* bytes */
+  int64_t num_pages;
+  int page_size, h_k, head_size; /* head_size a multiple of 16 */
+  const int32_t* src_pages;     /* (num_out_pages,) */
+  int64_t num_out_pages;
+  void* k_out;                  /* e4m3 logical (>= num_out_pages, page_size, h_k, head_size) */
+  void* v_out;
+  int64_t ko_stride_page, ko_stride_row, ko_stride_head; /* bytes */
+  int64_t vo_stride_page, vo_stride_row, vo_stride_head; /* bytes */
+  const float* k_ratio;         /* optional, per k_ratio_mode */
+  int k_ratio_mode;             /* MJ_SCALE_TENSOR | _HEAD | _CHANNEL */
+  const float* v_ratio;
+  int v_ratio_mode;
+  int32_t* status;              /* optional device status word (MJ_DEV_*) */
+} mj_expand_args;
+
+int mj_expand_pages(const mj_expand_args* args, void* stream);
+
 /* mj_decode for callers that cannot allocate device memory. No counterpart
  * in the reference. Engines that pre-size all of HBM into their own pools,
  * code issuing work during a global-mode stream capture (where cudaMalloc is

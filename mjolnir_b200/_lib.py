@@ -43,7 +43,7 @@ MJ_SCALE_CHANNEL = 2
 MJ_SCALE_SEQ_HEAD = 3
 
 EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine",
-            "mj_decode_noalloc", "mj_decode_kernel")
+            "mj_decode_noalloc", "mj_decode_kernel", "mj_expand_pages")
 
 _i64, _i32, _vp, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
 
@@ -61,6 +61,23 @@ class CacheWriteArgs(C.Structure):
         ("slot_mapping", _vp),
         ("k_scale", _vp), ("k_scale_mode", _i32),
         ("v_scale", _vp), ("v_scale_mode", _i32),
+        ("status", _vp),
+    ]
+
+
+class ExpandArgs(C.Structure):
+    _fields_ = [
+        ("k_cache", _vp), ("v_cache", _vp),
+        ("k_stride_page", _i64), ("k_stride_row", _i64), ("k_stride_head", _i64),
+        ("v_stride_page", _i64), ("v_stride_row", _i64), ("v_stride_head", _i64),
+        ("num_pages", _i64),
+        ("page_size", _i32), ("h_k", _i32), ("head_size", _i32),
+        ("src_pages", _vp), ("num_out_pages", _i64),
+        ("k_out", _vp), ("v_out", _vp),
+        ("ko_stride_page", _i64), ("ko_stride_row", _i64), ("ko_stride_head", _i64),
+        ("vo_stride_page", _i64), ("vo_stride_row", _i64), ("vo_stride_head", _i64),
+        ("k_ratio", _vp), ("k_ratio_mode", _i32),
+        ("v_ratio", _vp), ("v_ratio_mode", _i32),
         ("status", _vp),
     ]
 
@@ -125,6 +142,8 @@ def load():
             getattr(lib, fn).restype = C.c_int
         lib.mj_decode_kernel.argtypes = [C.POINTER(DecodeArgs)]
         lib.mj_decode_kernel.restype = C.c_int
+        lib.mj_expand_pages.argtypes = [C.POINTER(ExpandArgs), _vp]
+        lib.mj_expand_pages.restype = C.c_int
         _lib = lib
     return _lib
 
@@ -159,3 +178,8 @@ def decode_noalloc(args: DecodeArgs, stream: int) -> None:
     """mj_decode with the split-KV partials kept in the library's built-in
     16 MiB device array, for callers that cannot allocate device memory."""
     check(load().mj_decode_noalloc(C.byref(args), _vp(stream)))
+
+
+def expand_pages(args: ExpandArgs, stream: int) -> None:
+    """e2m3 -> e4m3 expansion of cache pages into a fallback's scratch."""
+    check(load().mj_expand_pages(C.byref(args), _vp(stream)))

@@ -12,6 +12,7 @@ cudaError_t launch_decode_simt(const mj_decode_args& a, cudaStream_t stream);
 cudaError_t launch_combine(const mj_decode_args& a, cudaStream_t stream);
 cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool* handled);
 const char* tc_ineligible(const mj_decode_args& a);
+cudaError_t launch_expand_pages(const mj_expand_args& a, cudaStream_t stream);
 }  // namespace mj
 
 static thread_local char g_err[512] = "";
@@ -152,6 +153,35 @@ int mj_combine(const mj_decode_args* args, void* stream) {
     return MJ_OK;
   }
   return cuda_status(mj::launch_combine(a, (cudaStream_t)stream), "mj_combine launch");
+}
+
+int mj_expand_pages(const mj_expand_args* args, void* stream) {
+  if (!args) return fail(MJ_ERR_INVALID, "mj_expand_pages: null args");
+  const mj_expand_args& a = *args;
+  if (a.num_out_pages < 0 || a.h_k <= 0 || a.page_size <= 0 || a.num_pages <= 0)
+    return fail(MJ_ERR_INVALID, "mj_expand_pages: num_out_pages %lld h_k %d page_size %d num_pages %lld",
+                (long long)a.num_out_pages, a.h_k, a.page_size, (long long)a.num_pages);
+  if (a.head_size <= 0 || a.head_size % 16)
+    return fail(MJ_ERR_UNSUPPORTED, "mj_expand_pages: head_size %d (a multiple of 16)", a.head_size);
+  if (a.num_out_pages == 0) {
+    g_err[0] = 0;
+    return MJ_OK;
+  }
+  if (!a.k_cache || !a.v_cache || !a.k_out || !a.v_out || !a.src_pages)
+    return fail(MJ_ERR_INVALID, "mj_expand_pages: null pointer argument");
+  for (int m : {a.k_ratio_mode, a.v_ratio_mode})
+    if (m != MJ_SCALE_TENSOR && m != MJ_SCALE_HEAD && m != MJ_SCALE_CHANNEL)
+      return fail(MJ_ERR_INVALID, "mj_expand_pages: ratio mode %d", m);
+  const int64_t in_strides[6] = {a.k_stride_page, a.k_stride_row, a.k_stride_head,
+                                 a.v_stride_page, a.v_stride_row, a.v_stride_head};
+  const int64_t out_strides[6] = {a.ko_stride_page, a.ko_stride_row, a.ko_stride_head,
+                                  a.vo_stride_page, a.vo_stride_row, a.vo_stride_head};
+  bool ok = aligned(a.k_cache, 4) && aligned(a.v_cache, 4) && aligned(a.k_out, 16) && aligned(a.v_out, 16);
+  for (int i = 0; i < 6; ++i) ok = ok && in_strides[i] % 4 == 0 && out_strides[i] % 16 == 0;
+  if (!ok) return fail(MJ_ERR_UNSUPPORTED, "mj_expand_pages: packed rows must be 4-byte and output rows 16-byte aligned");
+  if (a.num_out_pages * a.page_size * a.h_k > (int64_t)INT32_MAX)
+    return fail(MJ_ERR_UNSUPPORTED, "mj_expand_pages: too many rows");
+  return cuda_status(mj::launch_expand_pages(a, (cudaStream_t)stream), "mj_expand_pages launch");
 }
 
 }  // extern "C"

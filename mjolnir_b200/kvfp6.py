@@ -124,3 +124,55 @@ def write_kv(
     k_view = kv_cache[..., :rb].transpose(1, 2)
     v_view = kv_cache[..., rb:].transpose(1, 2)
     reshape_and_cache(key, value, k_view, v_view, slot_mapping, k_scale, v_scale, "e2m3")
+
+
+def expand_pages(
+    k_cache: torch.Tensor,  # e2m3 logical (pages, page_size, h_k, row_bytes) uint8 view
+    v_cache: torch.Tensor,
+    src_pages: torch.Tensor,  # (P,) int32: cache page of each output page
+    k_out: torch.Tensor,  # e4m3 logical (>= P, page_size, h_k, d) uint8 / float8 view
+    v_out: torch.Tensor,
+    k_ratio: torch.Tensor | None = None,  # fp32: 1 elem, (h_k,) or (h_k, d)
+    v_ratio: torch.Tensor | None = None,
+    status: torch.Tensor | None = None,
+) -> None:
+    """Expand P cache pages (K and V) to e4m3 bytes in output pages 0..P-1.
+
+    Without ratios the bytes are the e2m3 values exactly (the cache's scales
+    remain the descales). With per-channel scales s_c and a per-head descale S
+    of the reader, ratio = s_c / S makes each byte e4m3(code * s_c / S); a
+    reader without descales takes ratio = s_c (reference ``kvfp6.py:257-335``)."""
+    P = int(src_pages.shape[0])
+    if P == 0:
+        return
+    _, N, h_k, rb = k_cache.shape
+    d = rb * 4 // 3
+    if rb != row_bytes(d) or v_cache.shape != k_cache.shape:
+        raise ValueError(f"e2m3 views {tuple(k_cache.shape)} / {tuple(v_cache.shape)}")
+    for t in (k_out, v_out):
+        if t.dim() != 4 or t.shape[0] < P or tuple(t.shape[1:]) != (N, h_k, d) or t.element_size() != 1:
+            raise ValueError(f"output view {tuple(t.shape)} is not (>= {P}, {N}, {h_k}, {d}) bytes")
+    if src_pages.dtype != torch.int32:
+        src_pages = src_pages.to(torch.int32)
+    src_pages = src_pages.contiguous()
+    a = _lib.ExpandArgs()
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.k_stride_page, a.k_stride_row, a.k_stride_head = kv_byte_strides(k_cache)
+    a.v_stride_page, a.v_stride_row, a.v_stride_head = kv_byte_strides(v_cache)
+    a.num_pages, a.page_size, a.h_k, a.head_size = k_cache.shape[0], N, h_k, d
+    a.src_pages, a.num_out_pages = src_pages.data_ptr(), P
+    a.k_out, a.v_out = k_out.data_ptr(), v_out.data_ptr()
+    a.ko_stride_page, a.ko_stride_row, a.ko_stride_head = kv_byte_strides(k_out)
+    a.vo_stride_page, a.vo_stride_row, a.vo_stride_head = kv_byte_strides(v_out)
+    keep = []
+    for side, r in (("k", k_ratio), ("v", v_ratio)):
+        if r is None:
+            ptr, mode = None, _lib.MJ_SCALE_TENSOR
+        else:
+            r = r.to(torch.float32).contiguous()
+            keep.append(r)
+            ptr, mode = r.data_ptr(), scale_mode(r, h_k, d)
+        setattr(a, f"{side}_ratio", ptr)
+        setattr(a, f"{side}_ratio_mode", mode)
+    a.status = None if status is None else status.data_ptr()
+    _lib.expand_pages(a, _stream(k_cache.device))

@@ -62,7 +62,10 @@ class StepPlan:
 # ---------------------------------------------------------------------------
 # KV-cache views
 # ---------------------------------------------------------------------------
-KV_LAYOUTS = ("BHN2D", "BNH2D", "B2NHD", "B2HND", "2BNHD", "2BHND")
+# BHN2R is the (B, H, N, 2, row) shape the fp6 cache gets on a vLLM without
+# the pluggable KV-dtype API (see ``kvdtype``): BHN2D with K|V split into
+# their own dim, whatever stride order the fallback backend applied.
+KV_LAYOUTS = ("BHN2D", "BNH2D", "B2NHD", "B2HND", "2BNHD", "2BHND", "BHN2R")
 
 
 def detect_kv_layout(shape, num_kv_heads: int, page_size: int, head_size: int) -> str:
@@ -91,6 +94,8 @@ def detect_kv_layout(shape, num_kv_heads: int, page_size: int, head_size: int) -
             return "2BNHD"
         if s[0] == 2 and (s[2], s[3]) == (H, N):
             return "2BHND"
+        if s[3] == 2 and (s[1], s[2]) == (H, N):
+            return "BHN2R"
     raise ValueError(
         f"unrecognized KV cache shape {s} for H={H} N={N} D={D}; set MJOLNIR_ATTN_KV_LAYOUT to one of {KV_LAYOUTS}"
     )
@@ -112,6 +117,8 @@ def split_kv_cache(kv_cache: torch.Tensor, layout: str, row: int):
         k, v = kv_cache[0], kv_cache[1]
     elif layout == "2BHND":
         k, v = kv_cache[0].transpose(1, 2), kv_cache[1].transpose(1, 2)
+    elif layout == "BHN2R":
+        k, v = kv_cache[:, :, :, 0].transpose(1, 2), kv_cache[:, :, :, 1].transpose(1, 2)
     else:
         raise ValueError(layout)
     return k, v

@@ -182,3 +182,16 @@ def scale_mode(n: int, h_k: int, d: int) -> int:
         return 2
     assert n in (1, h_k)
     return 1 if n == h_k and h_k > 1 else 0
+
+
+def expand_rows_e4m3(packed: np.ndarray, d: int, ratio=None) -> np.ndarray:
+    """packed e2m3 rows (..., h_k, 3d/4) -> e4m3 bytes (..., h_k, d):
+    ``e4m3(code_value * ratio)`` with the product in float32, round to nearest
+    even, saturating at +-448; ratio None gives the code values exactly.
+    Restates the page expansion of reference ``kvfp6.py:157-205`` (the RATIO
+    branch of ``_expand_kernel``: value LUT x ratio, then the fp8 cast)."""
+    vals = decode_rows_e2m3(packed, d).astype(np.float32)
+    if ratio is not None:
+        h_k = packed.shape[-2]
+        vals = (vals * _expand_scale(ratio, h_k, d)).astype(np.float32)
+    return e4m3_bytes(vals)

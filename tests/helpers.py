@@ -21,6 +21,7 @@ LAYOUT_SHAPES = {
     "B2HND": lambda P, N, H, R: (P, 2, H, N, R),
     "2BNHD": lambda P, N, H, R: (2, P, N, H, R),
     "2BHND": lambda P, N, H, R: (2, P, H, N, R),
+    "BHN2R": lambda P, N, H, R: (P, H, N, 2, R),
 }
 
 

@@ -37,7 +37,7 @@ def test_struct_layouts_match_header():
 
     from mjolnir_b200 import _lib
 
-    src = '#include "mjolnir_b200.h"\n#include <stdio.h>\n#include <stddef.h>\nint main(){printf("%zu %zu %zu %zu\\n", sizeof(mj_cache_write_args), sizeof(mj_decode_args), offsetof(mj_decode_args, softmax_scale), offsetof(mj_cache_write_args, status));return 0;}\n'
+    src = '#include "mjolnir_b200.h"\n#include <stdio.h>\n#include <stddef.h>\nint main(){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(mj_cache_write_args), sizeof(mj_decode_args), offsetof(mj_decode_args, softmax_scale), offsetof(mj_cache_write_args, status), sizeof(mj_expand_args), offsetof(mj_expand_args, k_ratio));return 0;}\n'
     with tempfile.TemporaryDirectory() as d:
         c = os.path.join(d, "probe.c")
         open(c, "w").write(src)
@@ -49,6 +49,8 @@ def test_struct_layouts_match_header():
     assert sizes[1] == ctypes.sizeof(_lib.DecodeArgs)
     assert sizes[2] == _lib.DecodeArgs.softmax_scale.offset
     assert sizes[3] == _lib.CacheWriteArgs.status.offset
+    assert sizes[4] == ctypes.sizeof(_lib.ExpandArgs)
+    assert sizes[5] == _lib.ExpandArgs.k_ratio.offset
 
 
 def test_validation_errors_without_gpu():
@@ -67,3 +69,8 @@ def test_validation_errors_without_gpu():
     w.num_tokens, w.h_k, w.head_size, w.kv_format = 1, 1, 128, 7
     with pytest.raises(_lib.MjolnirError):
         _lib.cache_write(w, 0)
+    x = _lib.ExpandArgs()
+    x.num_out_pages, x.h_k, x.page_size, x.num_pages, x.head_size = 1, 1, 16, 1, 120
+    with pytest.raises(_lib.MjolnirError, match="head_size 120") as e:
+        _lib.expand_pages(x, 0)
+    assert e.value.code == _lib.MJ_ERR_UNSUPPORTED
