@@ -353,7 +353,13 @@ def main():
                                q_mul=wl.q_mul, o_mul=wl.o_mul)
     da.with_combine = 0
     combine = wl.plan.with_reduction
-    gathered = torch.empty(world, wl.T, wl.h_q * wl.d, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    if world > 1:
+        from mjolnir_b200.tp import gather_heads
+
+        # the all-gather buffer and the re-interleaved (T, h_q, d) output, fixed addresses
+        gbuf = torch.empty(world, wl.T, wl.h_q, wl.d, dtype=torch.bfloat16, device=dev)
+        full_out = torch.empty(wl.T, world * wl.h_q, wl.d, dtype=torch.bfloat16, device=dev)
+        local_out = wl.out.view(wl.T, wl.h_q, wl.d)
     launches_per_step = 2 + int(combine)
 
     def step(ev=None):
@@ -366,7 +372,7 @@ def main():
         if combine:
             _lib.combine(da, stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, wl.out)
+            gather_heads(local_out, world, buf=gbuf, out=full_out)
 
     def barrier():
         if world > 1:
@@ -398,7 +404,7 @@ def main():
     q_h = wl.query.cpu().pin_memory()
     k_h = wl.new_k.cpu().pin_memory()
     v_h = wl.new_v.cpu().pin_memory()
-    o_h = torch.empty((world * wl.T, wl.h_q * wl.d) if world > 1 else wl.out.shape, dtype=torch.bfloat16).pin_memory()
+    o_h = torch.empty((wl.T, world * wl.h_q * wl.d) if world > 1 else wl.out.shape, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
         wl.query.copy_(q_h, non_blocking=True)
@@ -407,8 +413,8 @@ def main():
         kvfp6.reshape_and_cache(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt)
         wl.runner.run(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale, q_mul=wl.q_mul, o_mul=wl.o_mul)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, wl.out)
-            o_h.copy_(gathered.view(world * wl.T, -1), non_blocking=True)
+            gather_heads(local_out, world, buf=gbuf, out=full_out)
+            o_h.copy_(full_out.view(wl.T, -1), non_blocking=True)
         else:
             o_h.copy_(wl.out, non_blocking=True)
 

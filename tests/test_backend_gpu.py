@@ -68,7 +68,7 @@ def test_write_then_decode_through_the_impl(kv_cache_dtype, q_len, tmp_path, mon
     g = torch.Generator().manual_seed(21)
     lens = [1 + q_len + 37, 300, 129]
     B = len(lens)
-    width = 32
+    width = 20  # 3 x 20 of the 64 pages; 300 tokens need 19
     perm = torch.randperm(64, generator=g)[: B * width].to(torch.int32)
     bt = perm.reshape(B, width)
     cache = torch.zeros(shape, dtype=torch.uint8, device="cuda")
