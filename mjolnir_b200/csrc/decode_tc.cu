@@ -74,7 +74,7 @@ struct Cfg {
   static constexpr int QBYTES = NS * 128;                // one K-major Q operand
   static constexpr int PBYTES = NO * 128;                // one MN-major P operand: NO/16 groups of [128 s][16 B]
   static constexpr int STAGES = NQP <= 8 ? 3 : 2;
-  static constexpr int TCOLS = 2 * NS + 2 * NO;          // S0 S1 O0 O1
+  static constexpr int TCOLS = 2 * NS + NO;              // S0 S1 O (O accumulates over a job's tiles)
   static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : 256;
   static_assert(TCOLS <= 256, "two CTAs per SM share the 512 TMEM columns");
   static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
@@ -92,7 +92,8 @@ struct Cfg {
 
 struct Bars {
   uint64_t *k_full, *k_empty, *v_full, *v_empty;               // TMA rings
-  uint64_t *s_full, *s_free, *p_full, *o_full, *o_free, *v_ready, *v_free, *q_full;  // pairs
+  uint64_t *s_full, *s_free, *p_full, *o_full, *v_ready, *v_free, *q_full;  // pairs (o_full: PV of tile t done)
+  uint64_t* o_free;                                         // once per job: O read out, next job may overwrite
   uint64_t* drain;
 };
 
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&b.s_free[i], 128);
       mbar_init(&b.p_full[i], 128);
       mbar_init(&b.o_full[i], 1);
-      mbar_init(&b.o_free[i], 128);
+      if (i == 0) mbar_init(b.o_free, 128);
       // e2m3: converter warps and softmax warpgroup share the V conversion
       mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? 64 + 128 : 64);
       mbar_init(&b.v_free[i], 1);
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S0 [0,NS) S1 [NS,2NS) O0 [2NS,2NS+NO) O1 [2NS+NO,2NS+2NO)
+  const uint32_t tmem = *tmem_slot;  // S0 [0,NS) S1 [NS,2NS) O [2NS,2NS+NO)
 
   constexpr uint32_t ATOM = FUSED ? 2048u : 1024u;  // byte stride between 8-row swizzle atoms of K (or V)
   auto kbuf = [&](int st) { return FUSED ? sm + st * 2 * kTileBytes : sm + C::K_OFF + st * kTileBytes; };
@@ -350,23 +351,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 1u, (uint32_t)NO);  // V and P both MN-major
       bool ok = true;
       int it = 0, jc = 0;
-      // O_t^T = V_t^T . P_t^T for global tile t
-      auto pv = [&](int t) {
+      int jo = 0;  // jobs whose O accumulation has started
+      // O^T += V_t^T . P_t^T for global tile t; the first tile of a job starts
+      // the accumulator fresh, once the previous job's O has been read out
+      auto pv = [&](int t, bool first) {
         const int st = t % S;
+        if (first && !mbar_wait(b.o_free, (jo & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)) return false;
         if (!(mbar_wait(&b.p_full[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-              mbar_wait(&b.v_ready[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-              mbar_wait(&b.o_free[t & 1], ((t >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)))
+              mbar_wait(&b.v_ready[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS)))
           return false;
+        if (first) ++jo;
         tc_fence_after();
         const uint32_t vaddr = smem_addr(vbuf(st));
         const uint32_t paddr = smem_addr(pbuf(t & 1));
-        const uint32_t d = tmem + (uint32_t)(2 * NS + (t & 1) * NO);
+        const uint32_t d = tmem + (uint32_t)(2 * NS);
         // P^T is [128 s][16 B] per group of 16 rows: 8-row core matrices 128 B
         // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_f8f6f4(d, smem_desc_sw128(vaddr + 4 * ATOM * k, kTileBytes, ATOM), smem_desc_noswz(paddr + 512 * k, 128, 2048),
-                     idesc_o, k > 0);
+                     idesc_o, k > 0 || !first);
         mma_commit(&b.o_full[t & 1]);
         mma_commit(&b.v_empty[st]);
         mma_commit(&b.v_free[t & 1]);
@@ -393,9 +397,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                        idesc_s, k > 0);
           mma_commit(&b.s_full[it & 1]);
           if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
-          if (i >= 1) ok = pv(it - 1);
+          if (i >= 1) ok = pv(it - 1, i == 1);
         }
-        if (ok) ok = pv(it - 1);  // the job's last tile
+        if (ok) ok = pv(it - 1, n == 1);  // the job's last tile
       }
       if (!ok && !*abort_flag) give_up();
       mma_commit(b.drain);  // all issued MMAs complete before TMEM is released
@@ -463,19 +467,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       // (group rows g*NQP + r), split in 3 e4m3 terms
       const int row0 = g * NQP;
       float qv[NQP];
-      int lim[NQP];  // last visible key of each query row (-1: padding row)
       float qmax = 0.f;
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
         float x = 0.f;
-        lim[r] = -1;
         if (row0 + r < n_q) {
           const int qi = (row0 + r) / h_r, rr = (row0 + r) % h_r;
           const int64_t tok = (int64_t)seq * q_len + qi;
           const int qh = h * h_r + rr;
           x = load_elem(a.q, tok * a.q_stride_tok + qh * a.q_stride_head + t, a.q_dtype);
           if (a.q_mul) x *= a.q_mul[(int64_t)qh * 128 + t];
-          lim[r] = a.causal ? L - q_len + qi : L - 1;
         }
         qv[r] = x;
         qmax = fmaxf(qmax, fabsf(x));
@@ -501,60 +502,71 @@ __global__ void __launch_bounds__(kThreads, 2)
       ++jc;
 
       // Query rows in pairs (packed f32x2 math). m: running max in log2 units,
-      // raised lazily (see kRescaleLog2); mu: the max the exponent uses (0
-      // while a row has seen no key); cr / crp: corrections of the current /
-      // previous tile; l: this thread's partial row sums; oa: O accumulator.
+      // raised lazily (see kRescaleLog2); l: this thread's partial row sums.
+      // O accumulates in TMEM over the job's tiles (the PV MMA adds each tile);
+      // when a row's max is raised, its O columns are rescaled in place.
       constexpr int NP = NQP / 2;
-      float2 m2[NP], mu2[NP], l2[NP], cr2[NP], crp2[NP], oa2[NP];
+      float2 m2[NP], l2[NP];
 #pragma unroll
       for (int q = 0; q < NP; ++q) {
         m2[q] = make_float2(-INFINITY, -INFINITY);
-        mu2[q] = make_float2(0.f, 0.f);
         l2[q] = make_float2(0.f, 0.f);
-        cr2[q] = make_float2(1.f, 1.f);
-        crp2[q] = cr2[q];
-        oa2[q] = l2[q];
       }
-      int lim_min = INT_MAX;  // a tile ending at or before lim_min needs no causal mask
-#pragma unroll
-      for (int r = 0; r < NQP; ++r)
-        if (row0 + r < n_q) lim_min = min(lim_min, lim[r]);
       const float2 c2v = make_float2(c2, c2);
-      // fold the O tile of global tile tt into the register accumulator; crp
-      // holds that tile's correction (accumulator max -> the tile's max)
-      auto fold = [&](int tt) {
-        if (!mbar_wait(&b.o_full[tt & 1], (tt >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
-        tc_fence_after();
-        float ov[NO];
-        tmem_ld_cols<NO>(tmem + (uint32_t)(2 * NS + (tt & 1) * NO) + lane_base, ov);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&b.o_free[tt & 1]);
-#pragma unroll
-        for (int q = 0; q < NP; ++q) oa2[q] = ffma2(oa2[q], crp2[q], combine3x2<NQP>(ov, 2 * q));
+      auto lim_of = [&](int r) {  // last key query row r may see (-1: padding row)
+        const int R = row0 + r;
+        return R < n_q ? (a.causal ? L - q_len + R / h_r : L - 1) : -1;
       };
+      // the group's first row sees the fewest keys: a tile ending at or before
+      // its limit needs no causal mask
+      const int lim_min = lim_of(0);
+      const uint32_t o_taddr = tmem + (uint32_t)(2 * NS) + lane_base;
 
+      // Barrier phases. o_full[t & 1] completes once per tile t, and this role
+      // waits on it only now and then (a rescale, the job's end); the phase it
+      // waits for cannot alias: S_t was committed after PV_{t-2} was issued, so
+      // once S_t has landed every PV up to t-2 is complete (and PV_{t+1} needs
+      // P_{t+1}, not yet written). The same ordering frees P buffer t & 1.
       const int n = te - tb;
-      // Per tile: S_i -> P_i first, then fold O of tile i-1, so the PV MMA of
-      // tile i runs while this warpgroup works on tile i+1.
       for (int i = 0; i < n; ++i, ++it) {
         if (!mbar_wait(&b.s_full[it & 1], (it >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
         tc_fence_after();
-        float sv[NS];
-        tmem_ld_cols<NS>(tmem + (uint32_t)((it & 1) * NS) + lane_base, sv);
-        tmem_wait_ld();
+        float2 x2[NP];
+        const uint32_t s_taddr = tmem + (uint32_t)((it & 1) * NS) + lane_base;
+        if constexpr (NQP <= 8) {
+          float sv[NS];
+          tmem_ld_cols<NS>(s_taddr, sv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < NP; ++q) x2[q] = fmul2(combine3x2<NQP>(sv, 2 * q), c2v);
+        } else {  // 8 query rows at a time: columns r, NQP + r, 2 NQP + r
+#pragma unroll
+          for (int c = 0; c < NQP; c += 8) {
+            float hv[8], mv[8], lv[8];
+            tmem_ld8(s_taddr + c, hv);
+            tmem_ld8(s_taddr + NQP + c, mv);
+            tmem_ld8(s_taddr + 2 * NQP + c, lv);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+              const float2 hi = make_float2(hv[k], hv[k + 1]), mid = make_float2(mv[k], mv[k + 1]),
+                           lo = make_float2(lv[k], lv[k + 1]);
+              x2[(c + k) / 2] = fmul2(
+                  ffma2(lo, make_float2(0.00390625f, 0.00390625f), ffma2(mid, make_float2(0.0625f, 0.0625f), hi)), c2v);
+            }
+          }
+        }
         tc_fence_before();
         mbar_arrive(&b.s_free[it & 1]);
         const int j0 = (tb + i) * kTileRows, j = j0 + t;  // this thread's KV row
         const bool edge = j0 + kTileRows - 1 > lim_min;  // some row sees only part of this tile
-        float2 x2[NP];
         bool grow = false;
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
-          float2 v = fmul2(combine3x2<NQP>(sv, 2 * q), c2v);
-          if (edge) {
-            if (j > lim[2 * q]) v.x = -INFINITY;
-            if (j > lim[2 * q + 1]) v.y = -INFINITY;
+          float2 v = x2[q];
+          if (edge) {  // rare (the tiles at a causal tail): recompute the limits
+            if (j > lim_of(2 * q)) v.x = -INFINITY;
+            if (j > lim_of(2 * q + 1)) v.y = -INFINITY;
           }
           x2[q] = v;
           grow = grow || (v.x > m2[q].x + kRescaleLog2) || (v.y > m2[q].y + kRescaleLog2);
@@ -576,25 +588,35 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
           }
           named_bar_sync(1, 128);
+          float cc[NQP];  // correction of each row's earlier sums: 2^(m_old - m_new)
 #pragma unroll
           for (int r = 0; r < NQP; ++r) {
             const float mt = fmaxf(fmaxf(rd[r], rd[NQP + r]), fmaxf(rd[2 * NQP + r], rd[3 * NQP + r]));
             float& mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
-            float& ur = (r & 1) ? mu2[r >> 1].y : mu2[r >> 1].x;
             float& lr = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
-            float& cc = (r & 1) ? cr2[r >> 1].y : cr2[r >> 1].x;
+            cc[r] = 1.f;
             if (mt > mr) {
-              cc = mr == -INFINITY ? 0.f : exp2_approx(mr - mt);
-              lr *= cc;
+              cc[r] = mr == -INFINITY ? 0.f : exp2_approx(mr - mt);
+              lr *= cc[r];
               mr = mt;
-              ur = mt;
-            } else {
-              cc = 1.f;
             }
           }
-        } else {
+          if (i >= 1) {  // O holds tiles tb .. tb+i-1: once PV_{it-1} lands, scale its rows
+            if (!mbar_wait(&b.o_full[(it - 1) & 1], ((it - 1) >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag)
+              give_up();
+            tc_fence_after();
 #pragma unroll
-          for (int q = 0; q < NP; ++q) cr2[q] = make_float2(1.f, 1.f);
+            for (int c = 0; c < 3 * NQP; c += 8) {
+              float ov[8];
+              tmem_ld8(o_taddr + c, ov);
+              tmem_wait_ld();
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                if (c + k < 3 * NQP) ov[k] *= cc[(c + k) % NQP];
+              tmem_st8(o_taddr + c, ov);
+            }
+            tmem_wait_st();
+          }
         }
         // P: three e4m3 terms per row, this thread's KV row s = t packed as the
         // 16-byte row s of each MN-major group (N rows hi | mid | lo | padding)
@@ -604,8 +626,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float2 ps2 = make_float2(kPScale, kPScale);
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
-          const float2 d = fadd2(x2[q], make_float2(-mu2[q].x, -mu2[q].y));
-          const float2 pv = make_float2(exp2_approx(d.x), exp2_approx(d.y));  // masked -> 0
+          // a row that has seen no key keeps m = -inf and all its scores -inf:
+          // the floor makes their exponent -inf (p = 0) instead of NaN
+          const float2 d = fadd2(x2[q], make_float2(-fmaxf(m2[q].x, -3.0e38f), -fmaxf(m2[q].y, -3.0e38f)));
+          const float2 pv = make_float2(exp2_approx(d.x), exp2_approx(d.y));
           l2[q] = fadd2(l2[q], pv);
           uint16_t hb, mb, lb;
           split3x2(fmul2(pv, ps2), hb, mb, lb);
@@ -619,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int g = 0; g < NO / 16; ++g)
           *reinterpret_cast<uint4*>(pb + g * 2048 + t * 16) = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
         fence_proxy_async_smem();
+        tc_fence_before();  // orders a rescale's TMEM stores before PV_it
         mbar_arrive(&b.p_full[it & 1]);
         if (FMT == MJ_KV_E2M3) {  // this warpgroup's share of the V conversion
           const int st = it % S;
@@ -632,14 +657,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           fence_proxy_async_smem();
           mbar_arrive(&b.v_ready[it & 1]);
         }
-        if (i >= 1) fold(it - 1);
-#pragma unroll
-        for (int q = 0; q < NP; ++q) crp2[q] = cr2[q];
       }
       if (aborted) break;
-      fold(it - 1);
 
-      // ---- epilogue: l per query row (sum of the per-thread partials), outputs
+      // ---- epilogue: l per query row (sum of the per-thread partials), O from TMEM
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
         float x = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
@@ -647,6 +668,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
         if (lane == 0) lred[wq * NQP + r] = x;
       }
+      if (!mbar_wait(&b.o_full[(it - 1) & 1], ((it - 1) >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag)
+        give_up();
+      tc_fence_after();
+      float orow[NQP];  // this thread's head-dim element of every row: hi + mid / 16 + lo / 256
+#pragma unroll
+      for (int c = 0; c < NQP; c += 8) {
+        float hv[8], mv[8], lv[8];
+        tmem_ld8(o_taddr + c, hv);
+        tmem_ld8(o_taddr + NQP + c, mv);
+        tmem_ld8(o_taddr + 2 * NQP + c, lv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 8 && c + k < NQP; ++k) orow[c + k] = hv[k] + mv[k] * 0.0625f + lv[k] * 0.00390625f;
+      }
+      tc_fence_before();
+      mbar_arrive(b.o_free);  // the next job's first PV may overwrite O
       if (named_bar_or(1, 128, *abort_flag != 0)) {
         aborted = true;
         break;
@@ -665,7 +702,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int qi = R / h_r, rr = R % h_r;
             const int64_t tok = (int64_t)seq * q_len + qi;
             const int qh = h * h_r + rr;
-            float o = ((r & 1) ? oa2[r >> 1].y : oa2[r >> 1].x) * inv;
+            float o = orow[r] * inv;
             const float mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
             const float lse = lt > 0.f ? (mr + log2f(lt)) * kLn2 : -INFINITY;
             if (final_out) {
