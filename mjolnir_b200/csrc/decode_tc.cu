@@ -49,7 +49,6 @@ namespace tc {
 
 using namespace sm100;
 
-constexpr int kThreads = 256;   // 8 warps
 constexpr int kTileBytes = 128 * 128;  // one 128 x 128 byte operand tile (e2m3: 16U6 slots)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -63,20 +62,36 @@ constexpr float kPScale = 448.0f / 256.0f;
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpCvt0 = 2;   // warps 2-3: V conversion (e2m3) / tail zeroing (e4m3)
-constexpr int kWarpSm0 = 4;    // warps 4-7: softmax warpgroup
-constexpr int kCvtThreads = 64 + 128;  // threads that share an e2m3 V tile conversion
+constexpr int kWarpSm0 = 4;    // warps 4.. : NWG softmax warpgroups of 4 warps
 
-template <int FMT, int NQP>
+// A CTA runs NWG softmax warpgroups of NQP query rows each (RT = NWG * NQP
+// rows per job). One warpgroup: two CTAs per SM; several: one CTA per SM that
+// streams each KV tile once for all its rows.
+template <int FMT, int NQP, int NWG>
 struct Cfg {
-  // Query rows enter the MMAs as three row blocks (hi, mid, lo) of NQP rows.
-  static constexpr int NS = (3 * NQP + 7) / 8 * 8 < 16 ? 16 : (3 * NQP + 7) / 8 * 8;  // S MMA N (Q is K-major)
-  static constexpr int NO = (3 * NQP + 15) / 16 * 16;    // PV MMA N (P is MN-major: multiples of 16)
+  static constexpr int RT = NWG * NQP;
+  static constexpr int THREADS = 128 * (1 + NWG);
+  static constexpr int CTAS_PER_SM = NWG == 1 ? 2 : 1;
+  static constexpr int CVT_THREADS = 64 + 128 * NWG;     // threads that share an e2m3 V tile conversion
+  // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
+  // warpgroup w owns rows w * NQP .. of each block.
+  static constexpr int NS = (3 * RT + 7) / 8 * 8 < 16 ? 16 : (3 * RT + 7) / 8 * 8;  // S MMA N (Q is K-major)
+  static constexpr int NO = (3 * RT + 15) / 16 * 16;     // PV MMA N (P is MN-major: multiples of 16)
   static constexpr int QBYTES = NS * 128;                // one K-major Q operand
   static constexpr int PBYTES = NO * 128;                // one MN-major P operand: NO/16 groups of [128 s][16 B]
-  static constexpr int STAGES = NQP <= 8 ? 3 : 2;
+  static constexpr int STAGES = NWG == 1 ? (NQP <= 8 ? 3 : 2) : NWG == 2 ? 5 : 4;
   static constexpr int TCOLS = 2 * NS + NO;              // S0 S1 O (O accumulates over a job's tiles)
-  static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : 256;
-  static_assert(TCOLS <= 256, "two CTAs per SM share the 512 TMEM columns");
+  static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
+  static_assert(TCOLS * CTAS_PER_SM <= 512, "the CTAs of an SM share its 512 TMEM columns");
+  static_assert(NWG == 1 || NQP % 16 == 0, "several warpgroups write whole 16-row P groups");
+  // Register split (setmaxnreg) when the launch allocation (THREADS x 128 at
+  // one CTA per SM with 512 threads) is too tight for the softmax rows: the
+  // TMA / MMA / converter warpgroup keeps REG_LO, the softmax ones get REG_HI;
+  // 128 * REG_LO + 128 * NWG * REG_HI must fit THREADS x the launch registers
+  // (checked on the host before the first launch).
+  static constexpr int REG_LO = NWG == 3 ? 64 : 0;
+  static constexpr int REG_HI = NWG == 3 ? 144 : 0;
+  static constexpr int REG_POOL = 128 * REG_LO + 128 * NWG * REG_HI;
   static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
   // shared memory plan (offsets from the 1024-aligned dynamic shared memory base)
   static constexpr int K_OFF = 0;
@@ -85,9 +100,9 @@ struct Cfg {
   static constexpr int P_OFF = (Q_OFF + 2 * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
   static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;
   static constexpr int NBARS = 4 * STAGES + 2 * 8 + 1;  // k/v full/empty rings, 8 pairs, drain
-  static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[2][4][NQP]
-  static constexpr int MISC_OFF = RED_OFF + 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [4][NQP]
-  static constexpr int SMEM = MISC_OFF + 64 + 4 * 4 * NQP;
+  static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[NWG][2][4][NQP]
+  static constexpr int MISC_OFF = RED_OFF + NWG * 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [NWG][4][NQP]
+  static constexpr int SMEM = MISC_OFF + 64 + NWG * 4 * 4 * NQP;
 };
 
 struct Bars {
@@ -125,15 +140,16 @@ __device__ __forceinline__ void split3(float y0, float y1, uint16_t& hb, uint16_
   lb = f2_to_e4m3x2((r0 - mv.x) * 16.f, (r1 - mv.y) * 16.f);
 }
 
-// Stores the three-term split of rows r, r+1 (column t) into a K-major tile.
-template <int NQP>
+// Stores the three-term split of rows r, r+1 (column t) into a K-major tile
+// whose hi / mid / lo row blocks are RT rows each.
+template <int RT>
 __device__ __forceinline__ void store_split(unsigned char* buf, int r, int t, uint16_t hb, uint16_t mb, uint16_t lb) {
   buf[sw128_offset(r, t)] = (uint8_t)(hb & 0xFF);
   buf[sw128_offset(r + 1, t)] = (uint8_t)(hb >> 8);
-  buf[sw128_offset(NQP + r, t)] = (uint8_t)(mb & 0xFF);
-  buf[sw128_offset(NQP + r + 1, t)] = (uint8_t)(mb >> 8);
-  buf[sw128_offset(2 * NQP + r, t)] = (uint8_t)(lb & 0xFF);
-  buf[sw128_offset(2 * NQP + r + 1, t)] = (uint8_t)(lb >> 8);
+  buf[sw128_offset(RT + r, t)] = (uint8_t)(mb & 0xFF);
+  buf[sw128_offset(RT + r + 1, t)] = (uint8_t)(mb >> 8);
+  buf[sw128_offset(2 * RT + r, t)] = (uint8_t)(lb & 0xFF);
+  buf[sw128_offset(2 * RT + r + 1, t)] = (uint8_t)(lb >> 8);
 }
 
 // C TMEM columns (a multiple of 8) of this thread's lane -> v
@@ -177,12 +193,12 @@ namespace tc {
 // (pages, h_k, page_size, K row | V row)); the box lands as alternating 1 KB
 // K and V swizzle atoms, so both operands see an atom stride of 2048 B.
 // Otherwise K and V are separate boxes into separate tiles (atom stride 1024 B).
-template <int FMT, int NQP, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 2)
+template <int FMT, int NQP, int NWG, bool FUSED>
+__global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG>::CTAS_PER_SM)
     decode_tc_kernel(const __grid_constant__ mj_decode_args a, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
-  using C = Cfg<FMT, NQP>;
-  constexpr int NS = C::NS, NO = C::NO;
+  using C = Cfg<FMT, NQP, NWG>;
+  constexpr int NS = C::NS, NO = C::NO, RT = C::RT;
   constexpr int S = C::STAGES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw;  // 1024-aligned: the 128-byte swizzle atoms need it
@@ -192,12 +208,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
   const int h_k = a.h_k;
-  // A job is (work item, KV head, row group): a CTA serves at most NQP query
+  // A job is (work item, KV head, row group): a CTA serves at most RT query
   // rows; a larger GQA x draft group is cut into n_rg row groups whose jobs
   // are adjacent in the list, so CTAs reading the same KV stream run side by
   // side and the repeat reads hit L2.
   const int n_q_all = a.q_len * (a.h_q / h_k);
-  const int n_rg = (n_q_all + NQP - 1) / NQP;
+  const int n_rg = (n_q_all + RT - 1) / RT;
   const int total_jobs = a.num_work * h_k * n_rg;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
@@ -215,11 +231,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   b.v_free = b.v_ready + 2;
   b.q_full = b.v_free + 2;
   b.drain = b.q_full + 2;
-  float* red = reinterpret_cast<float*>(sm + C::RED_OFF);   // [2][4][NQP]
+  float* red_all = reinterpret_cast<float*>(sm + C::RED_OFF);   // [NWG][2][4][NQP]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::MISC_OFF + 4);
   int& never_abort = *reinterpret_cast<int*>(sm + C::MISC_OFF + 8);  // no one sets it: drains wait on time only
-  float* lred = reinterpret_cast<float*>(sm + C::MISC_OFF + 64);  // [4][NQP]
+  float* lred_all = reinterpret_cast<float*>(sm + C::MISC_OFF + 64);  // [NWG][4][NQP]
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -230,14 +246,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b.s_full[i], 1);
-      mbar_init(&b.s_free[i], 128);
-      mbar_init(&b.p_full[i], 128);
+      mbar_init(&b.s_free[i], 128 * NWG);
+      mbar_init(&b.p_full[i], 128 * NWG);
       mbar_init(&b.o_full[i], 1);
-      if (i == 0) mbar_init(b.o_free, 128);
-      // e2m3: converter warps and softmax warpgroup share the V conversion
-      mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? 64 + 128 : 64);
+      if (i == 0) mbar_init(b.o_free, 128 * NWG);
+      // e2m3: converter warps and softmax warpgroups share the V conversion
+      mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? C::CVT_THREADS : 64);
       mbar_init(&b.v_free[i], 1);
-      mbar_init(&b.q_full[i], 1);
+      mbar_init(&b.q_full[i], NWG);
     }
     mbar_init(b.drain, 1);
     *abort_flag = 0;
@@ -281,191 +297,202 @@ __global__ void __launch_bounds__(kThreads, 2)
     return te > tb;
   };
 
-  if (warp == kWarpTma) {
-    // ---------------------------------------------------------------- producer
-    const int PS = a.page_size;
-    const int P = kTileRows / PS;  // pages per tile; lane p < P loads page p
-    int it = 0, k_issued = 0, v_issued = 0;
-    bool ok = true;
-    for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
-      int seq, tb, te, split, h, g;
-      if (!job(p, seq, tb, te, split, h, g)) continue;
-      const int L = a.seq_lens[seq];
-      const int32_t* bt = a.block_table + (int64_t)seq * a.block_table_stride;
-      auto page_coord = [&](int tile) {
-        int pg = (int)a.num_pages;  // out of range -> the TMA zero-fills the box
-        const int row0 = tile * kTileRows + lane * PS;
-        if (lane < P && row0 < L) {
-          const int v = bt[row0 / PS];
-          if (v < 0 || (int64_t)v >= a.num_pages) flag(a.status, MJ_DEV_BAD_PAGE);
-          else pg = v;
-        }
-        return pg;
-      };
-      int pg_next = page_coord(tb);
-      for (int tile = tb; tile < te; ++tile, ++it) {
-        const int st = it % S;
-        const uint32_t par = ((it / S) & 1) ^ 1;
-        const int pg = pg_next;
-        if (tile + 1 < te) pg_next = page_coord(tile + 1);
-        if (FUSED) {  // one box per page: K and V rows together (the stage frees after PV)
-          if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) break;
-          if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * C::K_TX);
-          __syncwarp();
-          if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h);
-          k_issued = it + 1;
-          continue;
-        }
-        if (lane == 0) ok = mbar_wait(&b.k_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], C::K_TX);
-        __syncwarp();
-        if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg);
-        k_issued = it + 1;
-        if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], C::K_TX);
-        __syncwarp();
-        if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg);
-        v_issued = it + 1;
-      }
-    }
-    if (lane == 0) {
-      if (!ok && !*abort_flag) give_up();
-      if (*abort_flag) {  // every issued copy must land before the CTA may exit
-        for (int k = k_issued > S ? k_issued - S : 0; k < k_issued; ++k)
-          mbar_wait(&b.k_full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
-        for (int k = v_issued > S ? v_issued - S : 0; k < v_issued; ++k)
-          mbar_wait(&b.v_full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
-      }
-    }
-    __syncwarp();
-  } else if (warp == kWarpMma) {
-    // ------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_s = idesc_f8f6f4(FMT == MJ_KV_E2M3 ? 3u : 0u, 0u, 0u, 0u, (uint32_t)NS);
-      const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 1u, (uint32_t)NO);  // V and P both MN-major
+  if (warp < kWarpSm0) {
+    // the TMA / MMA / converter warpgroup
+    if constexpr (C::REG_LO > 0) setmaxnreg_dec<C::REG_LO>();
+    if (warp == kWarpTma) {
+      // ---------------------------------------------------------------- producer
+      const int PS = a.page_size;
+      const int P = kTileRows / PS;  // pages per tile; lane p < P loads page p
+      int it = 0, k_issued = 0, v_issued = 0;
       bool ok = true;
-      int it = 0, jc = 0;
-      int jo = 0;  // jobs whose O accumulation has started
-      // O^T += V_t^T . P_t^T for global tile t; the first tile of a job starts
-      // the accumulator fresh, once the previous job's O has been read out
-      auto pv = [&](int t, bool first) {
-        const int st = t % S;
-        if (first && !mbar_wait(b.o_free, (jo & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)) return false;
-        if (!(mbar_wait(&b.p_full[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-              mbar_wait(&b.v_ready[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS)))
-          return false;
-        if (first) ++jo;
-        tc_fence_after();
-        const uint32_t vaddr = smem_addr(vbuf(st));
-        const uint32_t paddr = smem_addr(pbuf(t & 1));
-        const uint32_t d = tmem + (uint32_t)(2 * NS);
-        // P^T is [128 s][16 B] per group of 16 rows: 8-row core matrices 128 B
-        // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f8f6f4(d, smem_desc_sw128(vaddr + 4 * ATOM * k, kTileBytes, ATOM), smem_desc_noswz(paddr + 512 * k, 128, 2048),
-                     idesc_o, k > 0 || !first);
-        mma_commit(&b.o_full[t & 1]);
-        mma_commit(&b.v_empty[st]);
-        mma_commit(&b.v_free[t & 1]);
-        return true;
-      };
       for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
         int seq, tb, te, split, h, g;
         if (!job(p, seq, tb, te, split, h, g)) continue;
-        ok = mbar_wait(&b.q_full[jc & 1], (jc >> 1) & 1, abort_flag, MJ_TC_WAIT_NS);
-        const uint32_t qaddr = smem_addr(qbuf(jc & 1));
-        ++jc;
-        const int n = te - tb;
-        for (int i = 0; ok && i < n; ++i, ++it) {  // S_i = K_i . Q^T, then PV of the tile before
+        const int L = a.seq_lens[seq];
+        const int32_t* bt = a.block_table + (int64_t)seq * a.block_table_stride;
+        auto page_coord = [&](int tile) {
+          int pg = (int)a.num_pages;  // out of range -> the TMA zero-fills the box
+          const int row0 = tile * kTileRows + lane * PS;
+          if (lane < P && row0 < L) {
+            const int v = bt[row0 / PS];
+            if (v < 0 || (int64_t)v >= a.num_pages) flag(a.status, MJ_DEV_BAD_PAGE);
+            else pg = v;
+          }
+          return pg;
+        };
+        int pg_next = page_coord(tb);
+        for (int tile = tb; tile < te; ++tile, ++it) {
           const int st = it % S;
-          ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-               mbar_wait(&b.s_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+          const uint32_t par = ((it / S) & 1) ^ 1;
+          const int pg = pg_next;
+          if (tile + 1 < te) pg_next = page_coord(tile + 1);
+          if (FUSED) {  // one box per page: K and V rows together (the stage frees after PV)
+            if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * C::K_TX);
+            __syncwarp();
+            if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h);
+            k_issued = it + 1;
+            continue;
+          }
+          if (lane == 0) ok = mbar_wait(&b.k_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t kaddr = smem_addr(kbuf(st));
-          const uint32_t d = tmem + (uint32_t)((it & 1) * NS);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
-                       idesc_s, k > 0);
-          mma_commit(&b.s_full[it & 1]);
-          if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
-          if (i >= 1) ok = pv(it - 1, i == 1);
+          if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], C::K_TX);
+          __syncwarp();
+          if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg);
+          k_issued = it + 1;
+          if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], C::K_TX);
+          __syncwarp();
+          if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg);
+          v_issued = it + 1;
         }
-        if (ok) ok = pv(it - 1, n == 1);  // the job's last tile
+      }
+      if (lane == 0) {
+        if (!ok && !*abort_flag) give_up();
+        if (*abort_flag) {  // every issued copy must land before the CTA may exit
+          for (int k = k_issued > S ? k_issued - S : 0; k < k_issued; ++k)
+            mbar_wait(&b.k_full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
+          for (int k = v_issued > S ? v_issued - S : 0; k < v_issued; ++k)
+            mbar_wait(&b.v_full[k % S], (k / S) & 1, &never_abort, MJ_TC_WAIT_NS);
+        }
+      }
+      __syncwarp();
+    } else if (warp == kWarpMma) {
+      // ------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        const uint32_t idesc_s = idesc_f8f6f4(FMT == MJ_KV_E2M3 ? 3u : 0u, 0u, 0u, 0u, (uint32_t)NS);
+        const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 1u, (uint32_t)NO);  // V and P both MN-major
+        bool ok = true;
+        int it = 0, jc = 0;
+        int jo = 0;  // jobs whose O accumulation has started
+        // O^T += V_t^T . P_t^T for global tile t; the first tile of a job starts
+        // the accumulator fresh, once the previous job's O has been read out
+        auto pv = [&](int t, bool first) {
+          const int st = t % S;
+          if (first && !mbar_wait(b.o_free, (jo & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)) return false;
+          if (!(mbar_wait(&b.p_full[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+                mbar_wait(&b.v_ready[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS)))
+            return false;
+          if (first) ++jo;
+          tc_fence_after();
+          const uint32_t vaddr = smem_addr(vbuf(st));
+          const uint32_t paddr = smem_addr(pbuf(t & 1));
+          const uint32_t d = tmem + (uint32_t)(2 * NS);
+          // P^T is [128 s][16 B] per group of 16 rows: 8-row core matrices 128 B
+          // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows
+  #pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f8f6f4(d, smem_desc_sw128(vaddr + 4 * ATOM * k, kTileBytes, ATOM), smem_desc_noswz(paddr + 512 * k, 128, 2048),
+                       idesc_o, k > 0 || !first);
+          mma_commit(&b.o_full[t & 1]);
+          mma_commit(&b.v_empty[st]);
+          mma_commit(&b.v_free[t & 1]);
+          return true;
+        };
+        for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
+          int seq, tb, te, split, h, g;
+          if (!job(p, seq, tb, te, split, h, g)) continue;
+          ok = mbar_wait(&b.q_full[jc & 1], (jc >> 1) & 1, abort_flag, MJ_TC_WAIT_NS);
+          const uint32_t qaddr = smem_addr(qbuf(jc & 1));
+          ++jc;
+          const int n = te - tb;
+          for (int i = 0; ok && i < n; ++i, ++it) {  // S_i = K_i . Q^T, then PV of the tile before
+            const int st = it % S;
+            ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+                 mbar_wait(&b.s_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t kaddr = smem_addr(kbuf(st));
+            const uint32_t d = tmem + (uint32_t)((it & 1) * NS);
+  #pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
+                         idesc_s, k > 0);
+            mma_commit(&b.s_full[it & 1]);
+            if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
+            if (i >= 1) ok = pv(it - 1, i == 1);
+          }
+          if (ok) ok = pv(it - 1, n == 1);  // the job's last tile
+        }
+        if (!ok && !*abort_flag) give_up();
+        mma_commit(b.drain);  // all issued MMAs complete before TMEM is released
+        mbar_wait(b.drain, 0, &never_abort, MJ_TC_WAIT_NS);
+      }
+      __syncwarp();
+    } else {
+      // ------------------------------------------------ V conversion / tail zero
+      const int ct = threadIdx.x - kWarpCvt0 * 32;  // 0..63
+      int it = 0;
+      bool ok = true;
+      for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
+        int seq, tb, te, split, h, g;
+        if (!job(p, seq, tb, te, split, h, g)) continue;
+        const int L = a.seq_lens[seq];
+        for (int tile = tb; tile < te; ++tile, ++it) {
+          const int st = it % S;
+          // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
+          ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+               mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+          if (!ok) break;
+          if (FMT == MJ_KV_E2M3) {
+            // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
+            // this role converts chunks ct, ct + CVT_THREADS, ...; the softmax
+            // warpgroup converts the others after publishing P
+            unsigned char* vb = vbuf(st);
+  #pragma unroll 2
+            for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
+              uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+              *q = e2m3x16_to_e4m3(*q);
+            }
+            // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
+          } else {
+            // e4m3 rows past the sequence end inside its last page may hold NaN
+            // bytes; NaN * 0 would poison O, so zero them (their P is 0)
+            const int valid = L - tile * kTileRows;
+            if (valid < kTileRows) {
+              const int r0 = valid > 0 ? valid : 0;
+              unsigned char* vb = vbuf(st);
+              for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64)
+                *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&b.v_ready[it & 1]);
+        }
       }
       if (!ok && !*abort_flag) give_up();
-      mma_commit(b.drain);  // all issued MMAs complete before TMEM is released
-      mbar_wait(b.drain, 0, &never_abort, MJ_TC_WAIT_NS);
     }
-    __syncwarp();
-  } else if (warp < kWarpSm0) {
-    // ------------------------------------------------ V conversion / tail zero
-    const int ct = threadIdx.x - kWarpCvt0 * 32;  // 0..63
-    int it = 0;
-    bool ok = true;
-    for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
-      int seq, tb, te, split, h, g;
-      if (!job(p, seq, tb, te, split, h, g)) continue;
-      const int L = a.seq_lens[seq];
-      for (int tile = tb; tile < te; ++tile, ++it) {
-        const int st = it % S;
-        // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
-        ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-             mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
-        if (!ok) break;
-        if (FMT == MJ_KV_E2M3) {
-          // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
-          // this role converts chunks ct, ct + kCvtThreads, ...; the softmax
-          // warpgroup converts the others after publishing P
-          unsigned char* vb = vbuf(st);
-#pragma unroll 2
-          for (int c = ct; c < kTileBytes / 16; c += kCvtThreads) {
-            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
-            *q = e2m3x16_to_e4m3(*q);
-          }
-          // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
-        } else {
-          // e4m3 rows past the sequence end inside its last page may hold NaN
-          // bytes; NaN * 0 would poison O, so zero them (their P is 0)
-          const int valid = L - tile * kTileRows;
-          if (valid < kTileRows) {
-            const int r0 = valid > 0 ? valid : 0;
-            unsigned char* vb = vbuf(st);
-            for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64)
-              *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
-          }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&b.v_ready[it & 1]);
-      }
-    }
-    if (!ok && !*abort_flag) give_up();
   } else {
-    // --------------------------------------------------- softmax warpgroup
-    const int t = threadIdx.x - kWarpSm0 * 32;  // 0..127: TMEM lane = KV row of a tile = head-dim index
-    const int wq = warp - kWarpSm0;             // TMEM lane quarter
+    if constexpr (C::REG_HI > 0) setmaxnreg_inc<C::REG_HI>();
+    // -------------------------------------------------- softmax warpgroups
+    const int sw = (warp - kWarpSm0) >> 2;            // this warpgroup: rows sw * NQP .. of the job's RT
+    const int t = (threadIdx.x - kWarpSm0 * 32) & 127;  // TMEM lane = KV row of a tile = head-dim index
+    const int wq = (warp - kWarpSm0) & 3;             // TMEM lane quarter
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t bar_id = 1 + sw;                   // this warpgroup's named barrier
+    float* red = red_all + sw * 8 * NQP;              // [2][4][NQP]
+    float* lred = lred_all + sw * 4 * NQP;            // [4][NQP]
+    const int col0 = sw * NQP;                        // this warpgroup's rows within each row block
     const int h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r;  // rows of the whole group
-    // Q rows past 3*NQP (padding to the MMA's N) stay zero for the whole kernel
-    for (int i = 0; i < 2; ++i)
-      for (int row = 3 * NQP; row < NS; ++row) qbuf(i)[sw128_offset(row, t)] = 0;
+    // Q rows past 3*RT (padding to the MMA's N) stay zero for the whole kernel
+    if (sw == 0)
+      for (int i = 0; i < 2; ++i)
+        for (int row = 3 * RT; row < NS; ++row) qbuf(i)[sw128_offset(row, t)] = 0;
     int it = 0, jc = 0;
     bool aborted = false;
     for (int p = blockIdx.x; !aborted && p < total_jobs; p += gridDim.x) {
       int seq, tb, te, split, h, g;
       if (!job(p, seq, tb, te, split, h, g)) continue;
       const int L = a.seq_lens[seq];
-      // ---- Q of this job: head-dim element t of each of its query rows
-      // (group rows g*NQP + r), split in 3 e4m3 terms
-      const int row0 = g * NQP;
+      // ---- Q of this job: head-dim element t of each of this warpgroup's
+      // query rows (group rows g*RT + sw*NQP + r), split in 3 e4m3 terms
+      const int row0 = g * RT + col0;
       float qv[NQP];
       float qmax = 0.f;
 #pragma unroll
@@ -483,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       qmax = warp_max_f32(qmax);
       if (lane == 0) red[wq] = qmax;
-      if (named_bar_or(1, 128, *abort_flag != 0)) break;
+      if (named_bar_or(bar_id, 128, *abort_flag != 0)) break;
       qmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
       const float qs = qmax > 0.f ? 224.f / qmax : 1.f;  // |q * qs| <= 224
       unsigned char* qb = qbuf(jc & 1);
@@ -491,13 +518,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int r = 0; r < NQP; r += 2) {
         uint16_t hb, mb, lb;
         split3(qv[r] * qs, qv[r + 1] * qs, hb, mb, lb);
-        store_split<NQP>(qb, r, t, hb, mb, lb);
+        store_split<RT>(qb, col0 + r, t, hb, mb, lb);
       }
       fence_proxy_async_smem();
       const float kd = descale_at(a.k_descale, a.k_descale_mode, seq, h, h_k);
       const float vd = descale_at(a.v_descale, a.v_descale_mode, seq, h, h_k);
       const float c2 = a.softmax_scale * kd * kLog2e / qs;  // S (in q*qs units) -> log2 units
-      if (named_bar_or(1, 128, *abort_flag != 0)) break;  // Q written and fenced, red[] read
+      if (named_bar_or(bar_id, 128, *abort_flag != 0)) break;  // Q written and fenced, red[] read
       if (t == 0) mbar_arrive(&b.q_full[jc & 1]);
       ++jc;
 
@@ -534,6 +561,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         float2 x2[NP];
         const uint32_t s_taddr = tmem + (uint32_t)((it & 1) * NS) + lane_base;
         if constexpr (NQP <= 8) {
+          static_assert(NWG == 1, "small row counts run one warpgroup");
           float sv[NS];
           tmem_ld_cols<NS>(s_taddr, sv);
           tmem_wait_ld();
@@ -543,9 +571,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int c = 0; c < NQP; c += 8) {
             float hv[8], mv[8], lv[8];
-            tmem_ld8(s_taddr + c, hv);
-            tmem_ld8(s_taddr + NQP + c, mv);
-            tmem_ld8(s_taddr + 2 * NQP + c, lv);
+            tmem_ld8(s_taddr + col0 + c, hv);
+            tmem_ld8(s_taddr + RT + col0 + c, mv);
+            tmem_ld8(s_taddr + 2 * RT + col0 + c, lv);
             tmem_wait_ld();
 #pragma unroll
             for (int k = 0; k < 8; k += 2) {
@@ -573,8 +601,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         // one barrier per tile: a uniform vote on "some score outgrew its row's
         // max" (or abort); only then do the rows exchange their tile maxima
-        if (named_bar_or(1, 128, grow || *abort_flag != 0)) {
-          if (named_bar_or(1, 128, *abort_flag != 0)) {
+        if (named_bar_or(bar_id, 128, grow || *abort_flag != 0)) {
+          if (named_bar_or(bar_id, 128, *abort_flag != 0)) {
             aborted = true;
             break;
           }
@@ -587,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               rd[wq * NQP + 2 * q + 1] = w1;
             }
           }
-          named_bar_sync(1, 128);
+          named_bar_sync(bar_id, 128);
           float cc[NQP];  // correction of each row's earlier sums: 2^(m_old - m_new)
 #pragma unroll
           for (int r = 0; r < NQP; ++r) {
@@ -605,24 +633,40 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (!mbar_wait(&b.o_full[(it - 1) & 1], ((it - 1) >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag)
               give_up();
             tc_fence_after();
+            if constexpr (NWG == 1) {  // the three row blocks are contiguous: 3 * NQP columns
 #pragma unroll
-            for (int c = 0; c < 3 * NQP; c += 8) {
-              float ov[8];
-              tmem_ld8(o_taddr + c, ov);
-              tmem_wait_ld();
+              for (int c = 0; c < 3 * NQP; c += 8) {
+                float ov[8];
+                tmem_ld8(o_taddr + c, ov);
+                tmem_wait_ld();
 #pragma unroll
-              for (int k = 0; k < 8; ++k)
-                if (c + k < 3 * NQP) ov[k] *= cc[(c + k) % NQP];
-              tmem_st8(o_taddr + c, ov);
+                for (int k = 0; k < 8; ++k)
+                  if (c + k < 3 * NQP) ov[k] *= cc[(c + k) % NQP];
+                tmem_st8(o_taddr + c, ov);
+              }
+            } else {  // this warpgroup's NQP columns of each row block
+#pragma unroll
+              for (int blk = 0; blk < 3; ++blk)
+#pragma unroll
+                for (int c = 0; c < NQP; c += 8) {
+                  float ov[8];
+                  tmem_ld8(o_taddr + blk * RT + col0 + c, ov);
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int k = 0; k < 8; ++k) ov[k] *= cc[c + k];
+                  tmem_st8(o_taddr + blk * RT + col0 + c, ov);
+                }
             }
             tmem_wait_st();
           }
         }
         // P: three e4m3 terms per row, this thread's KV row s = t packed as the
         // 16-byte row s of each MN-major group (N rows hi | mid | lo | padding)
-        uint32_t w[NO / 4];
+        // words of this thread's P bytes: term k of row r at byte k * NQP + r
+        constexpr int NW = NWG == 1 ? NO / 4 : 3 * NQP / 4;
+        uint32_t w[NW];
 #pragma unroll
-        for (int k = 0; k < NO / 4; ++k) w[k] = 0u;
+        for (int k = 0; k < NW; ++k) w[k] = 0u;
         const float2 ps2 = make_float2(kPScale, kPScale);
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
@@ -639,9 +683,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           w[(2 * NQP + r) >> 2] |= (uint32_t)lb << sh;
         }
         unsigned char* pb = pbuf(it & 1);
+        if constexpr (NWG == 1) {  // the whole operand row: groups 0 .. NO/16
 #pragma unroll
-        for (int g = 0; g < NO / 16; ++g)
-          *reinterpret_cast<uint4*>(pb + g * 2048 + t * 16) = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+          for (int g = 0; g < NO / 16; ++g)
+            *reinterpret_cast<uint4*>(pb + g * 2048 + t * 16) = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+        } else {  // this warpgroup's 16-row groups of each term block
+#pragma unroll
+          for (int k = 0; k < 3; ++k)
+#pragma unroll
+            for (int j = 0; j < NQP / 16; ++j) {
+              const int g = (k * RT + col0) / 16 + j, wi = (k * NQP + 16 * j) / 4;
+              *reinterpret_cast<uint4*>(pb + g * 2048 + t * 16) = make_uint4(w[wi], w[wi + 1], w[wi + 2], w[wi + 3]);
+            }
+        }
         fence_proxy_async_smem();
         tc_fence_before();  // orders a rescale's TMEM stores before PV_it
         mbar_arrive(&b.p_full[it & 1]);
@@ -650,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (!FUSED && !mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
           unsigned char* vb = vbuf(st);
 #pragma unroll 2
-          for (int c = 64 + t; c < kTileBytes / 16; c += kCvtThreads) {
+          for (int c = 64 + sw * 128 + t; c < kTileBytes / 16; c += C::CVT_THREADS) {
             uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
             *q = e2m3x16_to_e4m3(*q);
           }
@@ -675,16 +729,16 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int c = 0; c < NQP; c += 8) {
         float hv[8], mv[8], lv[8];
-        tmem_ld8(o_taddr + c, hv);
-        tmem_ld8(o_taddr + NQP + c, mv);
-        tmem_ld8(o_taddr + 2 * NQP + c, lv);
+        tmem_ld8(o_taddr + col0 + c, hv);
+        tmem_ld8(o_taddr + RT + col0 + c, mv);
+        tmem_ld8(o_taddr + 2 * RT + col0 + c, lv);
         tmem_wait_ld();
 #pragma unroll
         for (int k = 0; k < 8 && c + k < NQP; ++k) orow[c + k] = hv[k] + mv[k] * 0.0625f + lv[k] * 0.00390625f;
       }
       tc_fence_before();
       mbar_arrive(b.o_free);  // the next job's first PV may overwrite O
-      if (named_bar_or(1, 128, *abort_flag != 0)) {
+      if (named_bar_or(bar_id, 128, *abort_flag != 0)) {
         aborted = true;
         break;
       }
@@ -825,18 +879,19 @@ static bool make_map_fused(CUtensorMap* m, const mj_decode_args& a, int64_t page
   return r == CUDA_SUCCESS;
 }
 
-template <int FMT, int NQP, bool FUSED>
+template <int FMT, int NQP, int NWG, bool FUSED>
 static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream) {
-  const int smem = tc::Cfg<FMT, NQP>::SMEM;
-  static int slots = 0;  // resident CTAs on this device (set once: one process per GPU)
+  using C = tc::Cfg<FMT, NQP, NWG>;
+  auto kern = tc::decode_tc_kernel<FMT, NQP, NWG, FUSED>;
+  const int smem = C::SMEM;
+  static int slots = 0;  // resident CTAs on this device (set once: one process per GPU); -1: unusable
   if (!slots) {
-    cudaError_t e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     // without a carveout preference the occupancy is computed for a smaller
     // shared-memory partition and one CTA per SM would be assumed
-    e = cudaFuncSetAttribute(tc::decode_tc_kernel<FMT, NQP, FUSED>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             (int)cudaSharedmemCarveoutMaxShared);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     // resident CTAs per SM from the device limits: shared memory (with the
     // per-block reserve), registers, and the 512 TMEM columns of an SM
@@ -847,32 +902,48 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
     if ((e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&reserve, cudaDevAttrReservedSharedMemoryPerBlock, dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev)) != cudaSuccess) return e;
-    if ((e = cudaFuncGetAttributes(&fa, tc::decode_tc_kernel<FMT, NQP, FUSED>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
+    // a register split must fit the CTA's launch allocation, or the
+    // increasing warpgroups would wait for registers that never come
+    if (C::REG_POOL > fa.numRegs * C::THREADS) {
+      slots = -1;
+      return cudaErrorNotSupported;
+    }
     int occ = smem_sm / (smem + (int)fa.sharedSizeBytes + reserve);
-    const int regs_cta = ((fa.numRegs + 7) / 8) * 8 * tc::kThreads;
+    const int regs_cta = ((fa.numRegs + 7) / 8) * 8 * C::THREADS;
     occ = occ < regs_sm / regs_cta ? occ : regs_sm / regs_cta;
-    occ = occ < 512 / tc::Cfg<FMT, NQP>::TMEM_COLS ? occ : 512 / tc::Cfg<FMT, NQP>::TMEM_COLS;
-    occ = occ < 2 ? occ : 2;  // __launch_bounds__ min blocks
+    occ = occ < 512 / C::TMEM_COLS ? occ : 512 / C::TMEM_COLS;
+    occ = occ < C::CTAS_PER_SM ? occ : C::CTAS_PER_SM;  // __launch_bounds__ min blocks
     slots = sms * (occ > 0 ? occ : 1);
   }
+  if (slots < 0) return cudaErrorNotSupported;
   const int n_q = a.q_len * (a.h_q / a.h_k);
-  const int64_t jobs = (int64_t)a.num_work * a.h_k * ((n_q + NQP - 1) / NQP);
+  const int64_t jobs = (int64_t)a.num_work * a.h_k * ((n_q + C::RT - 1) / C::RT);
   const unsigned grid = (unsigned)(jobs < slots ? jobs : slots);
-  tc::decode_tc_kernel<FMT, NQP, FUSED><<<grid, tc::kThreads, smem, stream>>>(a, mk, mv);
+  kern<<<grid, C::THREADS, smem, stream>>>(a, mk, mv);
   return cudaGetLastError();
+}
+
+// Variant by query rows per KV head (n_q): one warpgroup of 4, 8 or 16 rows
+// (two CTAs per SM), or two / three warpgroups of 16 rows in one CTA per SM
+// that read each KV tile once for up to 48 rows (row groups of 48 beyond).
+template <int FMT, bool FUSED>
+static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
+                                cudaStream_t stream) {
+  if (n_q <= 4) return launch_tc_t<FMT, 4, 1, FUSED>(a, mk, mv, stream);
+  if (n_q <= 8) return launch_tc_t<FMT, 8, 1, FUSED>(a, mk, mv, stream);
+  if (n_q <= 16) return launch_tc_t<FMT, 16, 1, FUSED>(a, mk, mv, stream);
+  if (n_q <= 32) return launch_tc_t<FMT, 16, 2, FUSED>(a, mk, mv, stream);
+  cudaError_t e = launch_tc_t<FMT, 16, 3, FUSED>(a, mk, mv, stream);
+  if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, FUSED>(a, mk, mv, stream);
+  return e;
 }
 
 template <bool FUSED>
 static cudaError_t dispatch_nq(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream) {
-  if (a.kv_format == MJ_KV_E2M3) {
-    if (n_q <= 4) return launch_tc_t<MJ_KV_E2M3, 4, FUSED>(a, mk, mv, stream);
-    return n_q <= 8 ? launch_tc_t<MJ_KV_E2M3, 8, FUSED>(a, mk, mv, stream)
-                    : launch_tc_t<MJ_KV_E2M3, 16, FUSED>(a, mk, mv, stream);
-  }
-  if (n_q <= 4) return launch_tc_t<MJ_KV_FP8_E4M3, 4, FUSED>(a, mk, mv, stream);
-  return n_q <= 8 ? launch_tc_t<MJ_KV_FP8_E4M3, 8, FUSED>(a, mk, mv, stream)
-                  : launch_tc_t<MJ_KV_FP8_E4M3, 16, FUSED>(a, mk, mv, stream);
+  if (a.kv_format == MJ_KV_E2M3) return dispatch_fmt<MJ_KV_E2M3, FUSED>(a, n_q, mk, mv, stream);
+  return dispatch_fmt<MJ_KV_FP8_E4M3, FUSED>(a, n_q, mk, mv, stream);
 }
 
 // Launch the tensor-core decode when it can run these arguments; *handled

@@ -261,12 +261,17 @@ class DecodeRunner:
     # ------------------------------------------------------------------ plan
     def n_tiles(self, q_len: int) -> int:
         """CTA jobs per (work item, KV head): the tensor-core kernel serves up to
-        16 query rows per job and cuts larger GQA x draft groups into row groups."""
+        48 query rows per job and cuts larger GQA x draft groups into row groups."""
         n_q = q_len * self.h_r
-        return 1 if n_q <= 16 else -(-n_q // 16)
+        return 1 if n_q <= 48 else -(-n_q // 48)
+
+    def ctas(self, q_len: int) -> int:
+        """Resident CTAs per SM of the kernel variant for this q_len: two for
+        up to 16 query rows per KV head, one (several warpgroups) beyond."""
+        return self.ctas_per_sm if q_len * self.h_r <= 16 else 1
 
     def slots(self, q_len: int) -> int:
-        return max(1, (self.sm_count * self.ctas_per_sm) // (self.h_k * self.n_tiles(q_len)))
+        return max(1, (self.sm_count * self.ctas(q_len)) // (self.h_k * self.n_tiles(q_len)))
 
     def plan(
         self,
@@ -293,7 +298,7 @@ class DecodeRunner:
             self.h_k,
             self.n_tiles(q_len),
             self.sm_count,
-            ctas_per_sm=self.ctas_per_sm,
+            ctas_per_sm=self.ctas(q_len),
             max_splits=self.max_splits,
             pad_to=self._cap,
             rebalance=self.rebalance,

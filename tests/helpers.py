@@ -31,7 +31,7 @@ class Case:
 
     def __init__(self, *, seq_lens, q_len=1, h_q=8, h_k=2, d=128, page_size=16, kv_format="fp8",
                  layout="B2NHD", seed=0, descale="tensor", max_num_seqs=None, outliers=0.0, device="cuda",
-                 q_scale=1.0):
+                 q_scale=1.0, k_ramp=0.0):
         from mjolnir_b200.runner import detect_kv_layout, split_kv_cache
 
         g = torch.Generator().manual_seed(seed)
@@ -62,6 +62,15 @@ class Case:
                 m = torch.rand(x.shape, generator=g) < outliers
                 x = torch.where(m, x * 8, x)
             raw[side] = x
+        if k_ramp:
+            # K grows with the token position (x 1 .. 1 + k_ramp over each
+            # sequence): later tiles raise the running max, so the kernels
+            # rescale what they accumulated from earlier tiles
+            for s, nb in enumerate(n_blocks):
+                L = max(self.seq_lens[s], 1)
+                for bi in range(nb):
+                    pos = torch.arange(bi * page_size, (bi + 1) * page_size, dtype=torch.float32)
+                    raw["k"][bt[s, bi]] *= (1.0 + k_ramp * pos / L).view(page_size, 1, 1)
         if kv_format == "fp8":
             self.k_scale_w = self.v_scale_w = torch.ones(1)
         else:

@@ -115,6 +115,21 @@ def test_split_and_unsplit_agree(sm_count, kernel):
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"sm {sm_count}")
 
 
+@pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
+@pytest.mark.parametrize("q_len,h_q", [(1, 8), (2, 8), (1, 32), (3, 16), (6, 16), (8, 16), (5, 16)])
+def test_tc_rescale_in_later_tiles(kv_format, q_len, h_q):
+    """Scores that grow along the sequence make the running max rise after the
+    first tile, so O accumulated in TMEM is rescaled in place. Row counts
+    cover the one-warpgroup (4, 8, 16 rows), two- and three-warpgroup (24, 48
+    rows, 40 with padding rows) and row-group (64 rows) variants."""
+    c = Case(seq_lens=(2000, 700, 1290), q_len=q_len, h_q=h_q, h_k=2, kv_format=kv_format, layout="BHN2D",
+             seed=43 + q_len, k_ramp=2.5)
+    out, _, _ = c.run(kernel="tc", sm_count=8)  # few slots: long chunks, many tiles per job
+    ref, _ = c.oracle()
+    T = c.b * q_len
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"rescale {kv_format} n_q {q_len * h_q // 2}")
+
+
 def test_tc_config4_shape_row_groups():
     """BASELINE config 4 shape (64 q / 8 KV heads, q_len 6 causal: 48 rows per KV
     head in 3 row groups), e2m3, shortened context."""
