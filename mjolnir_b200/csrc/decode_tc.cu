@@ -489,24 +489,46 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
     for (int p = blockIdx.x; !aborted && p < total_jobs; p += gridDim.x) {
       int seq, tb, te, split, h, g;
       if (!job(p, seq, tb, te, split, h, g)) continue;
-      const int L = a.seq_lens[seq];
       // ---- Q of this job: head-dim element t of each of this warpgroup's
-      // query rows (group rows g*RT + sw*NQP + r), split in 3 e4m3 terms
+      // query rows (group rows g*RT + sw*NQP + r), split in 3 e4m3 terms.
+      // Every global read of the job start is issued before any is used (one
+      // memory round trip, not one per row): padding rows read row n_q - 1
+      // and are zeroed after.
+      const int L = a.seq_lens[seq];
+      const int nsp = a.n_splits[seq];
       const int row0 = g * RT + col0;
-      float qv[NQP];
+      float qv[NQP], qm[NQP];
+      const int64_t qbase = (int64_t)seq * q_len * a.q_stride_tok + (int64_t)h * h_r * a.q_stride_head + t;
+      auto qoff = [&](int r) {  // element offset of row r's head-dim element t
+        const int R = min(row0 + r, n_q - 1);
+        return qbase + (int64_t)(R / h_r) * a.q_stride_tok + (int64_t)(R % h_r) * a.q_stride_head;
+      };
+      auto moff = [&](int r) { return (int64_t)(h * h_r + min(row0 + r, n_q - 1) % h_r) * 128 + t; };
+      if (a.q_dtype == MJ_DT_BF16) {
+        const __nv_bfloat16* q16 = reinterpret_cast<const __nv_bfloat16*>(a.q);
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) qv[r] = __bfloat162float(q16[qoff(r)]);
+      } else if (a.q_dtype == MJ_DT_FP16) {
+        const __half* q16 = reinterpret_cast<const __half*>(a.q);
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) qv[r] = __half2float(q16[qoff(r)]);
+      } else {
+        const float* q32 = reinterpret_cast<const float*>(a.q);
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) qv[r] = q32[qoff(r)];
+      }
+      if (a.q_mul) {
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) qm[r] = a.q_mul[moff(r)];
+      } else {
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) qm[r] = 1.f;
+      }
       float qmax = 0.f;
 #pragma unroll
       for (int r = 0; r < NQP; ++r) {
-        float x = 0.f;
-        if (row0 + r < n_q) {
-          const int qi = (row0 + r) / h_r, rr = (row0 + r) % h_r;
-          const int64_t tok = (int64_t)seq * q_len + qi;
-          const int qh = h * h_r + rr;
-          x = load_elem(a.q, tok * a.q_stride_tok + qh * a.q_stride_head + t, a.q_dtype);
-          if (a.q_mul) x *= a.q_mul[(int64_t)qh * 128 + t];
-        }
-        qv[r] = x;
-        qmax = fmaxf(qmax, fabsf(x));
+        qv[r] = row0 + r < n_q ? qv[r] * qm[r] : 0.f;
+        qmax = fmaxf(qmax, fabsf(qv[r]));
       }
       qmax = warp_max_f32(qmax);
       if (lane == 0) red[wq] = qmax;
@@ -742,7 +764,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
         aborted = true;
         break;
       }
-      const bool final_out = a.n_splits[seq] <= 1;
+      const bool final_out = nsp <= 1;
       const float vscale = (FMT == MJ_KV_E2M3 ? 64.f : 1.f) * vd / kPScale;
       if (!final_out && (split >= a.max_splits || seq >= a.part_seqs || !a.o_part)) {
         if (t == 0) flag(a.status, MJ_DEV_BAD_SPLIT);
