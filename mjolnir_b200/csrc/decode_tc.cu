@@ -769,28 +769,52 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
       if (!final_out && (split >= a.max_splits || seq >= a.part_seqs || !a.o_part)) {
         if (t == 0) flag(a.status, MJ_DEV_BAD_SPLIT);
       } else {
+        // O rows: normalized, times the V channel scales (final) -- the o_mul
+        // reads are issued together, the dtype branch taken once per job
+        float o[NQP];
+        const int qi0 = row0 / h_r, rr0 = row0 % h_r;
+        auto qh_of = [&](int r) { return h * h_r + (rr0 + r) % h_r; };
+        auto tok_of = [&](int r) { return (int64_t)seq * q_len + qi0 + (rr0 + r) / h_r; };
 #pragma unroll
         for (int r = 0; r < NQP; ++r) {
-          if (row0 + r < n_q) {
-            const int R = row0 + r;  // row of the whole group
-            const float lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
-            const float inv = lt > 0.f ? vscale / lt : 0.f;
-            const int qi = R / h_r, rr = R % h_r;
-            const int64_t tok = (int64_t)seq * q_len + qi;
-            const int qh = h * h_r + rr;
-            float o = orow[r] * inv;
-            const float mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
-            const float lse = lt > 0.f ? (mr + log2f(lt)) * kLn2 : -INFINITY;
-            if (final_out) {
-              if (a.o_mul) o *= a.o_mul[(int64_t)qh * 128 + t];
-              store_elem(a.o, tok * a.o_stride_tok + qh * a.o_stride_head + t, a.o_dtype, o);
-              if (t == 0 && a.lse) a.lse[tok * a.h_q + qh] = lse;
-            } else {
-              const int64_t row = (((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + R;
-              a.o_part[row * 128 + t] = o;
-              if (t == 0) a.lse_part[row] = lse;
-            }
+          const float lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
+          o[r] = lt > 0.f ? orow[r] * __fdividef(vscale, lt) : 0.f;
+        }
+        if (final_out && a.o_mul) {
+          float om[NQP];
+#pragma unroll
+          for (int r = 0; r < NQP; ++r) om[r] = a.o_mul[(int64_t)qh_of(min(r, n_q - 1 - row0)) * 128 + t];
+#pragma unroll
+          for (int r = 0; r < NQP; ++r) o[r] *= om[r];
+        }
+        if (final_out) {
+          if (a.o_dtype == MJ_DT_BF16) {
+            __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(a.o);
+#pragma unroll
+            for (int r = 0; r < NQP; ++r)
+              if (row0 + r < n_q) o16[tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + t] = __float2bfloat16_rn(o[r]);
+          } else {
+#pragma unroll
+            for (int r = 0; r < NQP; ++r)
+              if (row0 + r < n_q) store_elem(a.o, tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + t, a.o_dtype, o[r]);
           }
+        } else {
+          const int64_t prow = (((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + row0;
+#pragma unroll
+          for (int r = 0; r < NQP; ++r)
+            if (row0 + r < n_q) a.o_part[(prow + r) * 128 + t] = o[r];
+        }
+        if (t < NQP && row0 + t < n_q) {  // LSE (natural log) of row t: thread t writes it
+          float lt = 0.f, mr = 0.f;
+#pragma unroll
+          for (int r = 0; r < NQP; ++r)
+            if (r == t) {
+              lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
+              mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
+            }
+          const float lse = lt > 0.f ? (mr + log2f(lt)) * kLn2 : -INFINITY;
+          if (!final_out) a.lse_part[(((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + row0 + t] = lse;
+          else if (a.lse) a.lse[tok_of(t) * a.h_q + qh_of(t)] = lse;
         }
       }
     }
