@@ -61,18 +61,22 @@ constexpr float kPScale = 448.0f / 256.0f;
 // warp roles
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
-constexpr int kWarpCvt0 = 2;   // warps 2-3: V conversion (e2m3) / tail zeroing (e4m3)
-constexpr int kWarpSm0 = 4;    // warps 4.. : NWG softmax warpgroups of 4 warps
+// warps 2-3 (and, with CVTW, a whole second warpgroup): V conversion (e2m3) /
+// tail zeroing (e4m3); then NWG softmax warpgroups of 4 warps
 
 // A CTA runs NWG softmax warpgroups of NQP query rows each (RT = NWG * NQP
 // rows per job). One warpgroup: two CTAs per SM; several: one CTA per SM that
-// streams each KV tile once for all its rows.
-template <int FMT, int NQP, int NWG>
+// streams each KV tile once for all its rows. CVTW = 1 adds a warpgroup of
+// converter warps so that the softmax warpgroup converts no V.
+template <int FMT, int NQP, int NWG, int CVTW>
 struct Cfg {
   static constexpr int RT = NWG * NQP;
-  static constexpr int THREADS = 128 * (1 + NWG);
+  static constexpr int SM0 = 4 * (1 + CVTW);             // first softmax warp
+  static constexpr int THREADS = 128 * (1 + CVTW + NWG);
   static constexpr int CTAS_PER_SM = NWG == 1 ? 2 : 1;
-  static constexpr int CVT_THREADS = 64 + 128 * NWG;     // threads that share an e2m3 V tile conversion
+  static constexpr int CVT_ROLE = 64 + 128 * CVTW;       // threads of the converter role
+  static constexpr bool SM_CONVERTS = FMT == MJ_KV_E2M3 && CVTW == 0;  // softmax warpgroups share the conversion
+  static constexpr int CVT_THREADS = CVT_ROLE + (SM_CONVERTS ? 128 * NWG : 0);  // threads that convert a V tile
   // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
   // warpgroup w owns rows w * NQP .. of each block.
   static constexpr int NS = (3 * RT + 7) / 8 * 8 < 16 ? 16 : (3 * RT + 7) / 8 * 8;  // S MMA N (Q is K-major)
@@ -84,14 +88,14 @@ struct Cfg {
   static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
   static_assert(TCOLS * CTAS_PER_SM <= 512, "the CTAs of an SM share its 512 TMEM columns");
   static_assert(NWG == 1 || NQP % 16 == 0, "several warpgroups write whole 16-row P groups");
-  // Register split (setmaxnreg) when the launch allocation (THREADS x 128 at
-  // one CTA per SM with 512 threads) is too tight for the softmax rows: the
-  // TMA / MMA / converter warpgroup keeps REG_LO, the softmax ones get REG_HI;
-  // 128 * REG_LO + 128 * NWG * REG_HI must fit THREADS x the launch registers
-  // (checked on the host before the first launch).
-  static constexpr int REG_LO = NWG == 3 ? 64 : 0;
-  static constexpr int REG_HI = NWG == 3 ? 144 : 0;
-  static constexpr int REG_POOL = 128 * REG_LO + 128 * NWG * REG_HI;
+  // Register split (setmaxnreg) when the launch allocation is too tight for
+  // the softmax rows (512 threads at one CTA per SM: 128 each; 384 threads at
+  // two: 80): the TMA / MMA / converter warpgroups keep REG_LO, the softmax
+  // ones get REG_HI. REG_POOL must fit THREADS x the launch registers (checked
+  // on the host before the first launch).
+  static constexpr int REG_LO = NWG == 3 ? 64 : CVTW ? 56 : 0;
+  static constexpr int REG_HI = NWG == 3 ? 144 : CVTW ? 128 : 0;
+  static constexpr int REG_POOL = 128 * REG_LO * (1 + CVTW) + 128 * NWG * REG_HI;
   static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
   // shared memory plan (offsets from the 1024-aligned dynamic shared memory base)
   static constexpr int K_OFF = 0;
@@ -193,11 +197,11 @@ namespace tc {
 // (pages, h_k, page_size, K row | V row)); the box lands as alternating 1 KB
 // K and V swizzle atoms, so both operands see an atom stride of 2048 B.
 // Otherwise K and V are separate boxes into separate tiles (atom stride 1024 B).
-template <int FMT, int NQP, int NWG, bool FUSED>
-__global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG>::CTAS_PER_SM)
+template <int FMT, int NQP, int NWG, int CVTW, bool FUSED>
+__global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQP, NWG, CVTW>::CTAS_PER_SM)
     decode_tc_kernel(const __grid_constant__ mj_decode_args a, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
-  using C = Cfg<FMT, NQP, NWG>;
+  using C = Cfg<FMT, NQP, NWG, CVTW>;
   constexpr int NS = C::NS, NO = C::NO, RT = C::RT;
   constexpr int S = C::STAGES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -251,7 +255,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
       mbar_init(&b.o_full[i], 1);
       if (i == 0) mbar_init(b.o_free, 128 * NWG);
       // e2m3: converter warps and softmax warpgroups share the V conversion
-      mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? C::CVT_THREADS : 64);
+      mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? C::CVT_THREADS : C::CVT_ROLE);
       mbar_init(&b.v_free[i], 1);
       mbar_init(&b.q_full[i], NWG);
     }
@@ -297,7 +301,51 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
     return te > tb;
   };
 
-  if (warp < kWarpSm0) {
+  // ---------------------------------------- V conversion / tail zero (thread ct)
+  auto convert_role = [&](const int ct) {
+    int it = 0;
+    bool ok = true;
+    for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
+      int seq, tb, te, split, h, g;
+      if (!job(p, seq, tb, te, split, h, g)) continue;
+      const int L = a.seq_lens[seq];
+      for (int tile = tb; tile < te; ++tile, ++it) {
+        const int st = it % S;
+        // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
+        ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+             mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+        if (!ok) break;
+        if (FMT == MJ_KV_E2M3) {
+          // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
+          // this role converts chunks ct, ct + CVT_THREADS, ...; without a
+          // converter warpgroup the softmax warpgroups convert the others
+          // after publishing P
+          unsigned char* vb = vbuf(st);
+#pragma unroll 2
+          for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
+            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+            *q = e2m3x16_to_e4m3(*q);
+          }
+          // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
+        } else {
+          // e4m3 rows past the sequence end inside its last page may hold NaN
+          // bytes; NaN * 0 would poison O, so zero them (their P is 0)
+          const int valid = L - tile * kTileRows;
+          if (valid < kTileRows) {
+            const int r0 = valid > 0 ? valid : 0;
+            unsigned char* vb = vbuf(st);
+            for (int c = r0 * 8 + ct; c < kTileRows * 8; c += C::CVT_ROLE)
+              *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&b.v_ready[it & 1]);
+      }
+    }
+    if (!ok && !*abort_flag) give_up();
+  };
+
+  if (warp < 4) {
     // the TMA / MMA / converter warpgroup
     if constexpr (C::REG_LO > 0) setmaxnreg_dec<C::REG_LO>();
     if (warp == kWarpTma) {
@@ -426,54 +474,18 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
       }
       __syncwarp();
     } else {
-      // ------------------------------------------------ V conversion / tail zero
-      const int ct = threadIdx.x - kWarpCvt0 * 32;  // 0..63
-      int it = 0;
-      bool ok = true;
-      for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
-        int seq, tb, te, split, h, g;
-        if (!job(p, seq, tb, te, split, h, g)) continue;
-        const int L = a.seq_lens[seq];
-        for (int tile = tb; tile < te; ++tile, ++it) {
-          const int st = it % S;
-          // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
-          ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-               mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
-          if (!ok) break;
-          if (FMT == MJ_KV_E2M3) {
-            // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
-            // this role converts chunks ct, ct + CVT_THREADS, ...; the softmax
-            // warpgroup converts the others after publishing P
-            unsigned char* vb = vbuf(st);
-  #pragma unroll 2
-            for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
-              uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
-              *q = e2m3x16_to_e4m3(*q);
-            }
-            // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
-          } else {
-            // e4m3 rows past the sequence end inside its last page may hold NaN
-            // bytes; NaN * 0 would poison O, so zero them (their P is 0)
-            const int valid = L - tile * kTileRows;
-            if (valid < kTileRows) {
-              const int r0 = valid > 0 ? valid : 0;
-              unsigned char* vb = vbuf(st);
-              for (int c = r0 * 8 + ct; c < kTileRows * 8; c += 64)
-                *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
-            }
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(&b.v_ready[it & 1]);
-        }
-      }
-      if (!ok && !*abort_flag) give_up();
+      convert_role(threadIdx.x - 64);  // warps 2-3: converter threads 0..63
     }
+  } else if (warp < C::SM0) {
+    // the second converter warpgroup: converter threads 64 .. CVT_ROLE - 1
+    if constexpr (C::REG_LO > 0) setmaxnreg_dec<C::REG_LO>();
+    convert_role(64 + (int)threadIdx.x - 128);
   } else {
     if constexpr (C::REG_HI > 0) setmaxnreg_inc<C::REG_HI>();
     // -------------------------------------------------- softmax warpgroups
-    const int sw = (warp - kWarpSm0) >> 2;            // this warpgroup: rows sw * NQP .. of the job's RT
-    const int t = (threadIdx.x - kWarpSm0 * 32) & 127;  // TMEM lane = KV row of a tile = head-dim index
-    const int wq = (warp - kWarpSm0) & 3;             // TMEM lane quarter
+    const int sw = (warp - C::SM0) >> 2;              // this warpgroup: rows sw * NQP .. of the job's RT
+    const int t = (threadIdx.x - C::SM0 * 32) & 127;    // TMEM lane = KV row of a tile = head-dim index
+    const int wq = warp & 3;                          // TMEM lane quarter (warp % 4)
     const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
     const uint32_t bar_id = 1 + sw;                   // this warpgroup's named barrier
     float* red = red_all + sw * 8 * NQP;              // [2][4][NQP]
@@ -721,12 +733,12 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG>::THREADS, Cfg<FMT, NQP, NWG
         fence_proxy_async_smem();
         tc_fence_before();  // orders a rescale's TMEM stores before PV_it
         mbar_arrive(&b.p_full[it & 1]);
-        if (FMT == MJ_KV_E2M3) {  // this warpgroup's share of the V conversion
+        if constexpr (C::SM_CONVERTS) {  // this warpgroup's share of the V conversion
           const int st = it % S;
           if (!FUSED && !mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) && !*abort_flag) give_up();
           unsigned char* vb = vbuf(st);
 #pragma unroll 2
-          for (int c = 64 + sw * 128 + t; c < kTileBytes / 16; c += C::CVT_THREADS) {
+          for (int c = C::CVT_ROLE + sw * 128 + t; c < kTileBytes / 16; c += C::CVT_THREADS) {
             uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
             *q = e2m3x16_to_e4m3(*q);
           }
@@ -925,11 +937,11 @@ static bool make_map_fused(CUtensorMap* m, const mj_decode_args& a, int64_t page
   return r == CUDA_SUCCESS;
 }
 
-template <int FMT, int NQP, int NWG, bool FUSED>
+template <int FMT, int NQP, int NWG, int CVTW, bool FUSED>
 static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream) {
-  using C = tc::Cfg<FMT, NQP, NWG>;
-  auto kern = tc::decode_tc_kernel<FMT, NQP, NWG, FUSED>;
+  using C = tc::Cfg<FMT, NQP, NWG, CVTW>;
+  auto kern = tc::decode_tc_kernel<FMT, NQP, NWG, CVTW, FUSED>;
   const int smem = C::SMEM;
   static int slots = 0;  // resident CTAs on this device (set once: one process per GPU); -1: unusable
   if (!slots) {
@@ -971,17 +983,29 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
 }
 
 // Variant by query rows per KV head (n_q): one warpgroup of 4, 8 or 16 rows
-// (two CTAs per SM), or two / three warpgroups of 16 rows in one CTA per SM
-// that read each KV tile once for up to 48 rows (row groups of 48 beyond).
+// (two CTAs per SM; e2m3 adds a converter warpgroup), or two / three
+// warpgroups of 16 rows in one CTA per SM that read each KV tile once for up
+// to 48 rows (row groups of 48 beyond). A variant whose register split the
+// launch cannot cover is skipped for the next one down.
+template <int FMT, int NQP, bool FUSED>
+static cudaError_t launch_one_wg(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
+                                 cudaStream_t stream) {
+  if constexpr (FMT == MJ_KV_E2M3) {
+    cudaError_t e = launch_tc_t<FMT, NQP, 1, 1, FUSED>(a, mk, mv, stream);
+    if (e != cudaErrorNotSupported) return e;
+  }
+  return launch_tc_t<FMT, NQP, 1, 0, FUSED>(a, mk, mv, stream);
+}
+
 template <int FMT, bool FUSED>
 static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
                                 cudaStream_t stream) {
-  if (n_q <= 4) return launch_tc_t<FMT, 4, 1, FUSED>(a, mk, mv, stream);
-  if (n_q <= 8) return launch_tc_t<FMT, 8, 1, FUSED>(a, mk, mv, stream);
-  if (n_q <= 16) return launch_tc_t<FMT, 16, 1, FUSED>(a, mk, mv, stream);
-  if (n_q <= 32) return launch_tc_t<FMT, 16, 2, FUSED>(a, mk, mv, stream);
-  cudaError_t e = launch_tc_t<FMT, 16, 3, FUSED>(a, mk, mv, stream);
-  if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, FUSED>(a, mk, mv, stream);
+  if (n_q <= 4) return launch_one_wg<FMT, 4, FUSED>(a, mk, mv, stream);
+  if (n_q <= 8) return launch_one_wg<FMT, 8, FUSED>(a, mk, mv, stream);
+  if (n_q <= 16) return launch_one_wg<FMT, 16, FUSED>(a, mk, mv, stream);
+  if (n_q <= 32) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
+  cudaError_t e = launch_tc_t<FMT, 16, 3, 0, FUSED>(a, mk, mv, stream);
+  if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
   return e;
 }
 

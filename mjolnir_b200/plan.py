@@ -18,8 +18,10 @@ reference does not split at all, which on 148 SMs leaves a ragged last wave
 (e.g. 64 sequences x 8 KV heads = 512 CTAs = 1.73 waves of 296). The planner
 then evaluates every chunk size ceil(T / k), k = 1 .. max_splits, with a
 longest-first wave model -- the sum over waves of the longest item in each
-wave, plus a per-item overhead -- and keeps the cheapest. ``rebalance=False``
-reproduces the reference plan exactly.
+wave, plus a per-item overhead -- and keeps the cheapest. The overhead
+(2 tiles) is the tensor-core kernel's measured per-job cost: preparing the
+job's Q and writing its O / partials take about as long as two 128-row tiles.
+``rebalance=False`` reproduces the reference plan exactly.
 """
 
 from __future__ import annotations
@@ -80,7 +82,7 @@ def plan_split_kv(
     min_chunk_tiles: int = 1,
     pad_to: int = 0,
     rebalance: bool = True,
-    item_overhead: float = 0.5,
+    item_overhead: float = 2.0,
 ) -> SplitPlan:
     tiles = [max(1, math.ceil(int(L) / TILE_ROWS)) for L in seq_lens]
     T = max(tiles)
