@@ -47,6 +47,8 @@ WORKLOADS = {
     "cfg3": dict(h_q=32, h_k=8, d=128, b=128, q_len=1, L="lognormal", kv="e2m3", PS=16),
     "cfg4": dict(h_q=64, h_k=8, d=128, b=32, q_len=6, L=32768, kv="e2m3", PS=16),
     "cfg5": dict(h_q=64, h_k=8, d=128, b=256, q_len=1, L=131072, kv="e2m3", PS=16),
+    # the north-star target shape: Qwen3-8B e2m3 decode, batch 128 x 32K context
+    "ns": dict(h_q=32, h_k=8, d=128, b=128, q_len=1, L=32768, kv="e2m3", PS=16),
 }
 
 
@@ -352,7 +354,7 @@ def main():
     da = wl.runner.decode_args(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale,
                                q_mul=wl.q_mul, o_mul=wl.o_mul)
     da.with_combine = 0
-    combine = wl.plan.with_reduction
+    combine = wl.plan.with_reduction and not wl.runner.merges_in_kernel(da)
     if world > 1:
         from mjolnir_b200.tp import gather_heads
 

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define MJ_ABI_VERSION 1
+#define MJ_ABI_VERSION 2
 
 /* status codes */
 #define MJ_OK 0
@@ -160,6 +160,15 @@ typedef struct mj_decode_args {
   int with_combine;    /* also run mj_combine after the decode */
   int kernel;          /* MJ_KERNEL_AUTO, MJ_KERNEL_SIMT or MJ_KERNEL_TC */
   int32_t* status;     /* optional device status word (MJ_DEV_*) */
+  /* Optional (num_seqs * h_k * 64) int32 counters, zero before the first
+   * call; the kernel leaves them zero again. With them, the tensor-core
+   * kernel merges the split partials itself: the last job of each (sequence,
+   * KV head, row group) to finish merges them and writes the final O / LSE,
+   * so no mj_combine launch is needed (mj_decode skips it). Applies to the
+   * variants of up to 16 query rows per KV head with max_splits <= 16; the
+   * others, and the CUDA-core kernel, ignore the counters. Replaces the reference's planned last-CTA merge
+   * (arch/thor/decode.py:1417-1469, plan.py:122-129). */
+  int32_t* merge_counters;
 } mj_decode_args;
 
 int mj_decode(const mj_decode_args* args, void* stream);

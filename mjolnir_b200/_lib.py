@@ -104,6 +104,7 @@ class DecodeArgs(C.Structure):
         ("softmax_scale", _f32), ("causal", _i32), ("with_combine", _i32),
         ("kernel", _i32),
         ("status", _vp),
+        ("merge_counters", _vp),
     ]
 
 

@@ -57,6 +57,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 // p <= 2^kRescaleLog2 and p * kPScale <= 448 fits e4m3.
 constexpr float kRescaleLog2 = 8.0f;
 constexpr float kPScale = 448.0f / 256.0f;
+// the in-kernel split merge holds one partial per split in registers
+constexpr int kMergeMaxSplits = 16;
 
 // warp roles
 constexpr int kWarpTma = 0;
@@ -778,15 +780,15 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       }
       const bool final_out = nsp <= 1;
       const float vscale = (FMT == MJ_KV_E2M3 ? 64.f : 1.f) * vd / kPScale;
+      const int qi0 = row0 / h_r, rr0 = row0 % h_r;
+      auto qh_of = [&](int r) { return h * h_r + (rr0 + r) % h_r; };
+      auto tok_of = [&](int r) { return (int64_t)seq * q_len + qi0 + (rr0 + r) / h_r; };
       if (!final_out && (split >= a.max_splits || seq >= a.part_seqs || !a.o_part)) {
         if (t == 0) flag(a.status, MJ_DEV_BAD_SPLIT);
       } else {
         // O rows: normalized, times the V channel scales (final) -- the o_mul
         // reads are issued together, the dtype branch taken once per job
         float o[NQP];
-        const int qi0 = row0 / h_r, rr0 = row0 % h_r;
-        auto qh_of = [&](int r) { return h * h_r + (rr0 + r) % h_r; };
-        auto tok_of = [&](int r) { return (int64_t)seq * q_len + qi0 + (rr0 + r) / h_r; };
 #pragma unroll
         for (int r = 0; r < NQP; ++r) {
           const float lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
@@ -827,6 +829,63 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           const float lse = lt > 0.f ? (mr + log2f(lt)) * kLn2 : -INFINITY;
           if (!final_out) a.lse_part[(((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + row0 + t] = lse;
           else if (a.lse) a.lse[tok_of(t) * a.h_q + qh_of(t)] = lse;
+        }
+      }
+      // In-kernel split merge (one warpgroup per CTA, whose threads all take
+      // the same path): every job of a split (sequence, KV head, row group)
+      // counts itself in; the last one merges the partials and writes the
+      // final O / LSE, and puts the counter back to zero for the next launch.
+      if constexpr (NWG == 1) {
+        if (!final_out && a.merge_counters && a.max_splits <= kMergeMaxSplits) {
+          __threadfence();  // this job's partials, visible device-wide before it counts
+          named_bar_sync(bar_id, 128);
+          int* last_flag = reinterpret_cast<int*>(sm + C::MISC_OFF + 12);
+          if (t == 0) {
+            int* ctr = a.merge_counters + ((int64_t)seq * h_k + h) * n_rg + g;
+            const int last = atomicAdd(ctr, 1) == nsp - 1;
+            if (last) atomicExch(ctr, 0);
+            *last_flag = last;
+          }
+          named_bar_sync(bar_id, 128);
+          if (*last_flag && seq < a.part_seqs) {
+            __threadfence();
+            // every partial LSE of the group's rows, one per thread, into shared
+            // memory; then each thread merges its head-dim element of every row,
+            // the O partial reads of a row issued together
+            constexpr int MAXS = kMergeMaxSplits;
+            const int ns = min(nsp, a.max_splits);
+            const int64_t stride = (int64_t)a.part_seqs * h_k * n_q;
+            const int64_t base = ((int64_t)seq * h_k + h) * n_q + row0;
+            // scratch: the P buffer of tile it - 2, whose PV completed (PBYTES >= MAXS * NQP * 4)
+            float* lsm = reinterpret_cast<float*>(sm + C::P_OFF + (it & 1) * C::PBYTES);
+            for (int i = t; i < ns * NQP; i += 128) {
+              const int k = i / NQP, r = i % NQP;
+              lsm[i] = row0 + r < n_q ? __ldcg(a.lse_part + k * stride + base + r) : -INFINITY;
+            }
+            named_bar_sync(bar_id, 128);
+            for (int r = 0; r < NQP; ++r) {
+              if (row0 + r >= n_q) break;
+              float m = -INFINITY;
+              for (int k = 0; k < ns; ++k) m = fmaxf(m, lsm[k * NQP + r]);
+              float ov[MAXS];
+#pragma unroll
+              for (int k = 0; k < MAXS; ++k) ov[k] = k < ns ? __ldcg(a.o_part + (k * stride + base + r) * 128 + t) : 0.f;
+              float den = 0.f, acc = 0.f;
+              if (m != -INFINITY) {
+#pragma unroll
+                for (int k = 0; k < MAXS; ++k)
+                  if (k < ns) {
+                    const float w = __expf(lsm[k * NQP + r] - m);
+                    den += w;
+                    acc = fmaf(w, ov[k], acc);
+                  }
+              }
+              float o = den > 0.f ? acc / den : 0.f;
+              if (a.o_mul) o *= a.o_mul[(int64_t)qh_of(r) * 128 + t];
+              store_elem(a.o, tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + t, a.o_dtype, o);
+              if (t == 0 && a.lse) a.lse[tok_of(r) * a.h_q + qh_of(r)] = den > 0.f ? m + __logf(den) : -INFINITY;
+            }
+          }
         }
       }
     }

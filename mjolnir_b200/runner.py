@@ -215,6 +215,7 @@ class DecodeRunner:
         sm_count: int | None = None,
         rebalance: bool = True,
         kernel: str | None = None,
+        fused_merge: bool | None = None,
     ):
         if num_heads % num_kv_heads:
             raise ValueError("num_heads must be a multiple of num_kv_heads")
@@ -256,6 +257,15 @@ class DecodeRunner:
         self.o_part = torch.empty(part * head_size, dtype=torch.float32, device=dev)
         self.lse_part = torch.empty(part, dtype=torch.float32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        # split merge inside the tensor-core kernel (its last job per sequence
+        # and KV head merges; the counters return to zero after every launch).
+        # Off by default: it saves the combine launch but its fences, atomics
+        # and serial merges at the ends of jobs cost more on B200 (cfg2 decode
+        # 96 % -> 73 % of HBM, cfg3 81 % -> 74 %); MJOLNIR_ATTN_FUSED_MERGE=1.
+        if fused_merge is None:
+            fused_merge = env_flag("MJOLNIR_ATTN_FUSED_MERGE", "0").lower() in ("1", "true", "yes")
+        self.fused_merge = fused_merge
+        self.merge_counters = torch.zeros(max_num_seqs * self.h_k * 64, dtype=torch.int32, device=dev)
         self._one = torch.ones(1, dtype=torch.float32, device=dev)
 
     # ------------------------------------------------------------------ plan
@@ -386,7 +396,15 @@ class DecodeRunner:
         a.with_combine = int(plan.with_reduction)
         a.kernel = self.kernel
         a.status = self.status.data_ptr()
+        a.merge_counters = self.merge_counters.data_ptr() if self.fused_merge else None
         return a
+
+    def merges_in_kernel(self, args: _lib.DecodeArgs) -> bool:
+        """True when mj_decode merges the split partials inside the decode
+        launch (the one-warpgroup tensor-core variants given counters), so no
+        separate mj_combine launch is needed."""
+        return (bool(args.merge_counters) and self.kernel_name(args) == "decode_tc"
+                and args.q_len * (self.h_q // self.h_k) <= 16 and args.max_splits <= 16)
 
     def run(
         self,

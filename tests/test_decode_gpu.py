@@ -130,6 +130,28 @@ def test_tc_rescale_in_later_tiles(kv_format, q_len, h_q):
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"rescale {kv_format} n_q {q_len * h_q // 2}")
 
 
+@pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
+@pytest.mark.parametrize("q_len,h_q", [(1, 8), (2, 16), (4, 16)])
+def test_tc_in_kernel_merge_matches_combine_launch(kv_format, q_len, h_q):
+    """Split sequences: the last job of each (sequence, KV head) merges the
+    partials inside the decode launch; the result equals the separate merge
+    launch and the oracle, and stays right on a second launch (the counters
+    return to zero)."""
+    c = Case(seq_lens=(5000, 3000, 129, 900), q_len=q_len, h_q=h_q, h_k=2, kv_format=kv_format,
+             layout="BHN2D", seed=51 + q_len)
+    ref, _ = c.oracle()
+    T = c.b * q_len
+    outs = {}
+    for fused in (True, False):
+        for rep in range(2):
+            out, lse, plan = c.run(kernel="tc", fused_merge=fused, lse=True)
+            assert plan.with_reduction
+            assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"fused={fused} rep={rep}")
+        outs[fused] = (out[:T], lse)
+    assert torch.allclose(outs[True][0], outs[False][0], atol=1e-5, rtol=1e-5)
+    assert torch.allclose(outs[True][1], outs[False][1], atol=1e-4, rtol=1e-5)
+
+
 def test_tc_config4_shape_row_groups():
     """BASELINE config 4 shape (64 q / 8 KV heads, q_len 6 causal: 48 rows per KV
     head in 3 row groups), e2m3, shortened context."""
