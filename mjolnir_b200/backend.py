@@ -310,6 +310,10 @@ class MjolnirImpl(_BaseImpl):  # type: ignore[misc, valid-type]
             self.enable_cuda_graph = False
         self._kv_layout: str | None = None
         self._layer_reason = layer_reason(self)
+        # the kernel quantizes Q itself (three e4m3 terms per job): the layer
+        # keeps handing over bf16 Q; a fallback step that wants fp8 Q gets it
+        # quantized here, as the layer would (see _fallback_query)
+        self.supports_quant_query_input = False
 
     def fused_output_quant_supported(self, quant_key) -> bool:
         return False  # the kernel writes bf16 / fp16 output
@@ -377,6 +381,7 @@ class MjolnirImpl(_BaseImpl):  # type: ignore[misc, valid-type]
         **kwargs: Any,
     ):
         if not getattr(attn_metadata, "kernel_step", False):
+            query = self._fallback_query(layer, query, attn_metadata)
             if self._fp6 and attn_metadata is not None:
                 if getattr(attn_metadata, "mjolnir_fp6_pages", None) is None:
                     raise RuntimeError("Mjolnir: an fp6 fallback step without a page map (not built by MjolnirMetadataBuilder)")
@@ -411,6 +416,22 @@ class MjolnirImpl(_BaseImpl):  # type: ignore[misc, valid-type]
         else:
             runner.run(md.plan, query, output, k_cache, v_cache, layer._k_scale, layer._v_scale, self.scale)
         return output
+
+    @staticmethod
+    def _fallback_query(layer, query, attn_metadata):
+        """The fallback's metadata may ask for fp8 Q (FlashInfer's TRTLLM
+        kernels with an fp8 cache): quantize with the layer's static q scale,
+        as the layer itself would have (reference ``backend.py:609-621``)."""
+        want = getattr(attn_metadata, "q_data_type", None)
+        if want is None or query.dtype == want or query.dtype not in (torch.bfloat16, torch.float16):
+            return query
+        if want not in (torch.float8_e4m3fn, torch.float8_e5m2):
+            return query.to(want)
+        lim = torch.finfo(want).max
+        scale = layer._q_scale.float()
+        n = query.shape[0]
+        q = query.reshape(n, scale.numel(), -1).float() / scale.reshape(1, -1, 1)
+        return q.clamp_(-lim, lim).to(want).view(query.shape)
 
     def _write_kv_in_forward(self, layer, key, value, kv_cache, md) -> None:
         """Only for fallbacks whose forward also writes the cache (older vLLM)."""

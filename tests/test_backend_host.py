@@ -365,3 +365,14 @@ def test_fallback_step_without_page_map_is_refused(backend):
     impl = _impl(backend, "fp6_e2m3")
     with pytest.raises(RuntimeError, match="page map"):
         impl.forward(None, None, None, None, None, types.SimpleNamespace(), output=None)
+
+
+def test_fallback_query_quantized_when_the_fallback_wants_fp8(backend):
+    layer = types.SimpleNamespace(_q_scale=torch.tensor([0.5]))
+    q = torch.randn(3, 4, 128).to(torch.bfloat16)
+    md = types.SimpleNamespace(q_data_type=torch.float8_e4m3fn)
+    q8 = backend.MjolnirImpl._fallback_query(layer, q, md)
+    assert q8.dtype == torch.float8_e4m3fn and q8.shape == q.shape
+    assert torch.allclose(q8.float() * 0.5, q.float(), rtol=0.07, atol=0.02)
+    assert backend.MjolnirImpl._fallback_query(layer, q, types.SimpleNamespace()) is q
+    assert backend.MjolnirImpl._fallback_query(layer, q, types.SimpleNamespace(q_data_type=torch.bfloat16)) is q

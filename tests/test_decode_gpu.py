@@ -152,6 +152,18 @@ def test_tc_in_kernel_merge_matches_combine_launch(kv_format, q_len, h_q):
     assert torch.allclose(outs[True][1], outs[False][1], atol=1e-4, rtol=1e-5)
 
 
+@pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
+@pytest.mark.parametrize("h_q,h_k", [(8, 1), (16, 2), (32, 4)])
+def test_tc_tensor_parallel_shards(kv_format, h_q, h_k):
+    """The per-rank head counts of config 5 under TP 8 / 4 / 2 (64 q / 8 KV
+    heads split by KV head): one KV head per rank included."""
+    c = Case(seq_lens=(3000, 17, 1290), h_q=h_q, h_k=h_k, kv_format=kv_format, layout="BHN2D", seed=61 + h_k)
+    out, _, _ = c.run(kernel="tc")
+    ref, _ = c.oracle()
+    T = c.b
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"tp shard {h_q}/{h_k}")
+
+
 def test_tc_config4_shape_row_groups():
     """BASELINE config 4 shape (64 q / 8 KV heads, q_len 6 causal: 48 rows per KV
     head in 3 row groups), e2m3, shortened context."""
