@@ -73,6 +73,21 @@ def uniform_q_len(query_start_loc_cpu, num_reqs: int, q_len: int) -> bool:
     return all(x == 0 for x in lens[n:])
 
 
+def fp8_view_of(spec):
+    """The KV spec as the fallback sees an fp6 cache: its quant mode fp8
+    (the pages it reads are the e4m3 scratch)."""
+    try:
+        from dataclasses import replace
+
+        from vllm.v1.kv_cache_interface import KVQuantMode
+    except ImportError:
+        return spec
+    mode = getattr(KVQuantMode, "FP8_PER_TENSOR", None)
+    if mode is None or not hasattr(spec, "kv_quant_mode"):
+        return spec
+    return replace(spec, kv_quant_mode=mode)
+
+
 class MjolnirMetadataBuilder(_BaseBuilder):  # type: ignore[misc, valid-type]
     # a shared-metadata shortcut across KV-cache groups would skip the plan
     supports_update_block_table: bool = False
@@ -81,14 +96,18 @@ class MjolnirMetadataBuilder(_BaseBuilder):  # type: ignore[misc, valid-type]
         cache_config = vllm_config.cache_config
         saved = cache_config.cache_dtype
         fp6 = kv_format(saved) == "e2m3"
+        base_spec = kv_cache_spec
         if fp6:
             # the fallback's builder maps the cache dtype for its kernels and
-            # only ever reads the e4m3 scratch: it is built as for fp8
+            # only ever reads the e4m3 scratch: it is built as for fp8 (the
+            # cache dtype and the spec's quant mode say fp8 while it runs)
             cache_config.cache_dtype = "fp8"
+            base_spec = fp8_view_of(kv_cache_spec)
         try:
-            super().__init__(kv_cache_spec, layer_names, vllm_config, device, *args, **kwargs)
+            super().__init__(base_spec, layer_names, vllm_config, device, *args, **kwargs)
         finally:
             cache_config.cache_dtype = saved
+        self.kv_cache_spec = kv_cache_spec
         self._setup(kv_cache_spec, layer_names, vllm_config, device)
 
     def _setup(self, kv_cache_spec, layer_names, vllm_config, device) -> None:

@@ -60,6 +60,7 @@ def test_vllm_generates_on_the_kernel(tmp_path):
             doc = json.loads(scales.read_text())
             assert doc["format"] == "mjolnir.kv_scales/2" and len(doc["amax"]) == 2
     for kv, r in results.items():
+        print(kv, r["stats"], r["tokens"][0][:8])
         assert all(len(t) == 24 for t in r["tokens"]), kv
         assert r["stats"]["kernel_steps"] > 0, f"{kv}: no decode step ran on the kernel ({r['stats']})"
         assert r["stats"]["fallback_steps"] > 0, f"{kv}: the prefill should run on the fallback ({r['stats']})"

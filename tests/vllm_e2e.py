@@ -13,6 +13,8 @@ import json
 import os
 import sys
 
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
 
 def main() -> None:
     model_dir, kv, scales, calibrate, out_path = sys.argv[1:6]
