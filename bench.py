@@ -170,22 +170,28 @@ class Workload:
 # measurement helpers
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """`nvidia-smi` SM clocks and clock-event (throttle) reasons, sampled every
+    50 ms from before the warm-up until after the timed region. The summary
+    keeps the samples that arrived inside the timed region (marked with
+    `mark_start` / `mark_end`); a region shorter than the sampling period is
+    represented by the samples nearest to it. Reads settings only."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
-        self.lines = []
+        self.samples = []  # (arrival time, sm_mhz, max_mhz, reason names)
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
         except OSError:
@@ -193,11 +199,25 @@ class ClockSampler:
         return self
 
     def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        for ln in self.proc.stdout:
+            f = [x.strip() for x in ln.strip().split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                self.samples.append((time.monotonic(), float(f[1]), float(f[2]),
+                                     {n for n, v in zip(self.NAMES, f[5:9]) if v.lower() == "active"}))
+            except ValueError:
+                continue
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.15)  # the sample covering the end of the region
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -205,22 +225,19 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        smp = list(self.samples)
+        window = "timed region"
+        if self.t0 is not None and self.t1 is not None:
+            inside = [x for x in smp if self.t0 <= x[0] <= self.t1 + 0.1]
+            if not inside and smp:  # region shorter than the period: the nearest samples
+                before = [x for x in smp if x[0] < self.t0][-1:]
+                after = [x for x in smp if x[0] > self.t1][:1]
+                inside, window = before + after, "nearest to the timed region"
+            smp = inside
+        sm = [x[1] for x in smp]
+        reasons = set().union(*[x[3] for x in smp]) if smp else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smp[-1][2] if smp else None,
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 def peaks():
@@ -381,18 +398,24 @@ def main():
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    clk = ClockSampler(local)
+    clk.__enter__()  # sampling from before the warm-up, so the timed region has samples
+    try:
+        for _ in range(args.warmup):
+            step()
         barrier()
+        dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        clk.mark_start()
         t0.record()
         for i in range(args.steps):
             step(dec_ev[i])
         t1.record()
         barrier()
+        clk.mark_end()
+    finally:
+        clk.__exit__(None, None, None)
     ms = t0.elapsed_time(t1) / args.steps
     dec_ms = sum(a.elapsed_time(b) for a, b in dec_ev) / args.steps
     ms_t = torch.tensor([ms, dec_ms], device=dev)
