@@ -1,35 +1,38 @@
 // Paged split-KV decode attention on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA per (work item, KV head); a work item is a contiguous chunk of
-// 128-row KV tiles of one sequence (the planner's unit, the reference's
-// arch/thor/plan.py:140-197), and the CTA serves all n_q = q_len * h_r query
-// rows of the KV head from one read of each KV byte.
+// Persistent, warp-specialized CTAs walk a job list: a job is (work item, KV
+// head, row group), a work item a contiguous chunk of 128-row KV tiles of one
+// sequence (the planner's unit, the reference's arch/thor/plan.py:140-197).
+// A job serves RT = NWG x NQP query rows of the KV head (every query head of
+// the GQA group and every draft position) from one read of each KV byte.
 //
 // Data path per 128-row tile:
-//   TMA (one box per page, shuffled pages via the block table) -> SMEM ring,
+//   TMA (one box per page through the block table; for the (B, H, N, 2*row)
+//   layout one 5-D box lands the page's K and V rows together) -> SMEM ring,
 //   128-byte swizzled; e2m3 rows arrive through the 16U6 TMA type (12 packed
 //   bytes per 16-byte slot), e4m3 rows as bytes. Pages past the sequence are
 //   read at an out-of-range page coordinate: the TMA zero-fills them.
-//   S = K . Q^T        tcgen05.mma kind::f8f6f4, M = 128 KV rows, N = 3*NQP,
+//   S = K . Q^T        tcgen05.mma kind::f8f6f4, M = 128 KV rows, N = 3*RT,
 //                      A = K (e4m3 or e2m3, K-major), B = Q split in three
-//                      e4m3 terms (rows [0,NQP) = hi, [NQP,2NQP) = mid =
-//                      (q - hi) * 16, [2NQP,3NQP) = lo = (q - hi - mid/16) * 256)
-//   softmax            4 warps, thread = TMEM lane = KV row; base-2 online
-//                      softmax in fp32; P split the same way into three e4m3
-//                      terms (scaled by 448) and stored K-major for the next MMA
-//   O^T = V^T . P^T    tcgen05.mma kind::f8f6f4, M = 128 head-dim rows,
-//                      A = V (e4m3, MN-major), B = P; a fresh TMEM tile per KV
-//                      tile, folded into fp32 registers (thread = head-dim
-//                      lane) with the running-max correction
-//   e2m3 V cannot be an MN-major MMA operand, so two converter warps rewrite
-//   each 16-code slot in place as 16 e4m3 bytes of value code * 2^-6 (exact;
-//   the 2^6 is folded into the output scale).
+//                      e4m3 terms (row blocks hi, mid = (q - hi) * 16,
+//                      lo = (q - hi - mid/16) * 256, RT rows each)
+//   softmax            NWG warpgroups, thread = TMEM lane = KV row; base-2
+//                      online softmax in fp32 with a lazily raised max; P
+//                      split into three e4m3 terms (scaled by 448/256),
+//                      stored MN-major for the next MMA
+//   O^T += V^T . P^T   tcgen05.mma kind::f8f6f4, M = 128 head-dim rows,
+//                      A = V (e4m3, MN-major), B = P; O accumulates in TMEM
+//                      over the job's tiles and is rescaled in place on the
+//                      rare max raise, read out once at the job's end
+//   e2m3 V cannot be an MN-major MMA operand, so converter warps (a whole
+//   warpgroup in the one-warpgroup variants) rewrite each 16-code slot in
+//   place as 16 e4m3 bytes of value code * 2^-6 (exact; the 2^6 is folded
+//   into the output scale).
 //
 // Numerics: split-fp8 Q and P carry ~12 significant bits each
-// (hi + mid / 16 + lo / 256),
-// accumulation is fp32 in TMEM, softmax is fp32; the reference's
-// single-e4m3 recipe (arch/thor/decode.py:1288-1297) is not used because it
-// misses the 2e-3 tolerance.
+// (hi + mid / 16 + lo / 256), accumulation is fp32 in TMEM, softmax is fp32;
+// the reference's single-e4m3 recipe (arch/thor/decode.py:1288-1297) is not
+// used because it misses the 2e-3 tolerance.
 //
 // Every mbarrier wait is bounded (MJ_TC_WAIT_NS); on a timeout the CTA sets
 // MJ_DEV_TIMEOUT in the status word, all roles stop at their next wait, wait
