@@ -98,8 +98,8 @@ struct Cfg {
   // two: 80): the TMA / MMA / converter warpgroups keep REG_LO, the softmax
   // ones get REG_HI. REG_POOL must fit THREADS x the launch registers (checked
   // on the host before the first launch).
-  static constexpr int REG_LO = NWG == 3 ? 64 : CVTW ? 56 : 0;
-  static constexpr int REG_HI = NWG == 3 ? 144 : CVTW ? 128 : 0;
+  static constexpr int REG_LO = NWG == 3 ? (CVTW ? 48 : 64) : CVTW ? 56 : 0;
+  static constexpr int REG_HI = NWG == 3 ? (CVTW ? 128 : 144) : CVTW ? 128 : 0;
   static constexpr int REG_POOL = 128 * REG_LO * (1 + CVTW) + 128 * NWG * REG_HI;
   static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
   // shared memory plan (offsets from the 1024-aligned dynamic shared memory base)
@@ -606,21 +606,19 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < NP; ++q) x2[q] = fmul2(combine3x2<NQP>(sv, 2 * q), c2v);
-        } else {  // 8 query rows at a time: columns r, NQP + r, 2 NQP + r
+        } else {  // this warpgroup's columns r, RT + r, 2 RT + r of 16 query rows: one wait
+          static_assert(NQP == 16, "wide variants run 16 rows per warpgroup");
+          float hv[16], mv[16], lv[16];
+          tmem_ld16(s_taddr + col0, hv);
+          tmem_ld16(s_taddr + RT + col0, mv);
+          tmem_ld16(s_taddr + 2 * RT + col0, lv);
+          tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < NQP; c += 8) {
-            float hv[8], mv[8], lv[8];
-            tmem_ld8(s_taddr + col0 + c, hv);
-            tmem_ld8(s_taddr + RT + col0 + c, mv);
-            tmem_ld8(s_taddr + 2 * RT + col0 + c, lv);
-            tmem_wait_ld();
-#pragma unroll
-            for (int k = 0; k < 8; k += 2) {
-              const float2 hi = make_float2(hv[k], hv[k + 1]), mid = make_float2(mv[k], mv[k + 1]),
-                           lo = make_float2(lv[k], lv[k + 1]);
-              x2[(c + k) / 2] = fmul2(
-                  ffma2(lo, make_float2(0.00390625f, 0.00390625f), ffma2(mid, make_float2(0.0625f, 0.0625f), hi)), c2v);
-            }
+          for (int k = 0; k < 16; k += 2) {
+            const float2 hi = make_float2(hv[k], hv[k + 1]), mid = make_float2(mv[k], mv[k + 1]),
+                         lo = make_float2(lv[k], lv[k + 1]);
+            x2[k / 2] = fmul2(
+                ffma2(lo, make_float2(0.00390625f, 0.00390625f), ffma2(mid, make_float2(0.0625f, 0.0625f), hi)), c2v);
           }
         }
         tc_fence_before();
@@ -1066,7 +1064,9 @@ static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensor
   if (n_q <= 8) return launch_one_wg<FMT, 8, FUSED>(a, mk, mv, stream);
   if (n_q <= 16) return launch_one_wg<FMT, 16, FUSED>(a, mk, mv, stream);
   if (n_q <= 32) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
-  cudaError_t e = launch_tc_t<FMT, 16, 3, 0, FUSED>(a, mk, mv, stream);
+  cudaError_t e = cudaErrorNotSupported;
+  if constexpr (FMT == MJ_KV_E2M3) e = launch_tc_t<FMT, 16, 3, 1, FUSED>(a, mk, mv, stream);
+  if (e == cudaErrorNotSupported) e = launch_tc_t<FMT, 16, 3, 0, FUSED>(a, mk, mv, stream);
   if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
   return e;
 }
