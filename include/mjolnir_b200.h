@@ -181,6 +181,43 @@ int mj_decode_kernel(const mj_decode_args* args);
 int mj_combine(const mj_decode_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Split-KV planning on the host, and a runner handle that owns a decode's   */
+/* plan buffers, for hosts that drive the library without the Python runner. */
+/*                                                                            */
+/* mj_plan_split_kv replaces arch/thor/plan.py:140-197 `plan_split_kv` (plus */
+/* the B200 rebalance, rebalance != 0; item_overhead in tiles, 2.0 is the     */
+/* measured per-job cost): sequence lengths in, the work list (seq,          */
+/* tile_begin, tile_end, split) of 128-row tiles longest first and each      */
+/* sequence's split count out; pad_to > 0 pads the list with empty items.     */
+/* Pure host code, no CUDA call.                                             */
+int mj_plan_split_kv(const int32_t* seq_lens, int num_seqs, int h_k, int n_q_tiles, int sm_count, int ctas_per_sm,
+                     int max_splits, int pad_to, int rebalance, float item_overhead, int32_t* work_out,
+                     int work_capacity, int32_t* n_splits_out, int* num_work_out, int* chunk_tiles_out);
+
+/* The runner replaces the reference's T5DecodeRunner state                  */
+/* (arch/thor/runner.py:143-174, plan :184-234): mj_create allocates, on     */
+/* `device`, the fixed-address work list and split counts (a CUDA graph      */
+/* captured on one plan replays any later one), the split partials for       */
+/* max_splits x max_num_seqs x h_k x max_q_len x h_q / h_k rows, the status  */
+/* word and a pinned staging copy; NULL on failure (see mj_last_error).       */
+/* mj_plan plans host sequence lengths (+ margin tokens each) and copies the */
+/* plan asynchronously on `stream`; fixed_grid != 0 launches the padded      */
+/* capacity (graph capture). mj_runner_fill writes the plan's and buffers'   */
+/* fields (shapes, work, n_splits, num_work, partials, part_seqs, status,    */
+/* with_combine) into a mj_decode_args whose tensors the caller sets.         */
+/* mj_runner_status reads and clears the device status word (synchronous;   */
+/* returns MJ_DEV_* or a negative MJ_ERR_*). Calls on one runner are not     */
+/* thread-safe.                                                               */
+typedef struct mj_runner mj_runner;
+mj_runner* mj_create(int device, int h_q, int h_k, int head_size, int page_size, int max_num_seqs, int max_q_len,
+                     int kv_format, int max_splits, int ctas_per_sm);
+int mj_plan(mj_runner* runner, const int32_t* seq_lens_host, int num_seqs, int q_len, int margin, int fixed_grid,
+            void* stream);
+int mj_runner_fill(const mj_runner* runner, mj_decode_args* args);
+int mj_runner_status(mj_runner* runner);
+void mj_destroy(mj_runner* runner);
+
+/* ------------------------------------------------------------------------ */
 /* e2m3 -> e4m3 page expansion for steps a stock fallback backend runs on an */
 /* e2m3 cache. Replaces kvfp6.py:257-335 `expand_pages_to_fp8` (called from  */
 /* backend.py:573-607 on the page map of builder.py:479-509). Output page j  */

@@ -43,7 +43,8 @@ MJ_SCALE_CHANNEL = 2
 MJ_SCALE_SEQ_HEAD = 3
 
 EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine",
-            "mj_decode_noalloc", "mj_decode_kernel", "mj_expand_pages")
+            "mj_decode_noalloc", "mj_decode_kernel", "mj_expand_pages", "mj_plan_split_kv", "mj_create", "mj_plan",
+            "mj_runner_fill", "mj_runner_status", "mj_destroy")
 
 _i64, _i32, _vp, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
 
@@ -145,6 +146,20 @@ def load():
         lib.mj_decode_kernel.restype = C.c_int
         lib.mj_expand_pages.argtypes = [C.POINTER(ExpandArgs), _vp]
         lib.mj_expand_pages.restype = C.c_int
+        _pi = C.POINTER(C.c_int32)
+        lib.mj_plan_split_kv.argtypes = [_pi, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.c_float, _pi, C.c_int, _pi, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        lib.mj_plan_split_kv.restype = C.c_int
+        lib.mj_create.argtypes = [C.c_int] * 10
+        lib.mj_create.restype = _vp
+        lib.mj_plan.argtypes = [_vp, _pi, C.c_int, C.c_int, C.c_int, C.c_int, _vp]
+        lib.mj_plan.restype = C.c_int
+        lib.mj_runner_fill.argtypes = [_vp, C.POINTER(DecodeArgs)]
+        lib.mj_runner_fill.restype = C.c_int
+        lib.mj_runner_status.argtypes = [_vp]
+        lib.mj_runner_status.restype = C.c_int
+        lib.mj_destroy.argtypes = [_vp]
+        lib.mj_destroy.restype = None
         _lib = lib
     return _lib
 
@@ -184,3 +199,23 @@ def decode_noalloc(args: DecodeArgs, stream: int) -> None:
 def expand_pages(args: ExpandArgs, stream: int) -> None:
     """e2m3 -> e4m3 expansion of cache pages into a fallback's scratch."""
     check(load().mj_expand_pages(C.byref(args), _vp(stream)))
+
+
+def plan_split_kv(seq_lens, h_k: int, n_q_tiles: int, sm_count: int, ctas_per_sm: int = 1, max_splits: int = 16,
+                  pad_to: int = 0, rebalance: bool = True, item_overhead: float = 2.0):
+    """The library's host planner (mj_plan_split_kv): (work (n, 4) int32 array,
+    n_splits list, chunk_tiles)."""
+    import numpy as np
+
+    lens = np.ascontiguousarray(np.asarray(seq_lens, dtype=np.int32))
+    n = len(lens)
+    tiles = [max(1, -(-int(L) // 128)) for L in lens]
+    cap = max(pad_to, sum(tiles))
+    work = np.zeros((max(cap, 1), 4), dtype=np.int32)
+    ns = np.zeros(n, dtype=np.int32)
+    num, chunk = C.c_int(0), C.c_int(0)
+    _pi = C.POINTER(C.c_int32)
+    check(load().mj_plan_split_kv(lens.ctypes.data_as(_pi), n, h_k, n_q_tiles, sm_count, ctas_per_sm, max_splits,
+                                  pad_to, int(rebalance), float(item_overhead), work.ctypes.data_as(_pi), len(work),
+                                  ns.ctypes.data_as(_pi), C.byref(num), C.byref(chunk)))
+    return work[: num.value], ns.tolist(), chunk.value

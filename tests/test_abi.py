@@ -12,7 +12,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def _declared():
     src = open(os.path.join(ROOT, "include", "mjolnir_b200.h")).read()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(mj_\w+)\(", src, re.M)))
+    return sorted(set(re.findall(r"^(?:int|const char\*|void|mj_runner\*)\s+(mj_\w+)\(", src, re.M)))
 
 
 def test_header_symbols_exported():
@@ -20,7 +20,8 @@ def test_header_symbols_exported():
 
     lib = _lib.load()
     declared = _declared()
-    assert set(declared) >= {"mj_cache_write", "mj_decode", "mj_combine", "mj_last_error"}
+    assert set(declared) >= {"mj_cache_write", "mj_decode", "mj_combine", "mj_last_error", "mj_create", "mj_plan",
+                             "mj_runner_fill", "mj_destroy", "mj_plan_split_kv"}
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in include/mjolnir_b200.h but not exported"
     assert set(_lib.EXPORTED) <= set(declared)
@@ -74,3 +75,15 @@ def test_validation_errors_without_gpu():
     with pytest.raises(_lib.MjolnirError, match="head_size 120") as e:
         _lib.expand_pages(x, 0)
     assert e.value.code == _lib.MJ_ERR_UNSUPPORTED
+
+
+def test_runner_create_fails_cleanly_without_a_gpu_or_bad_shapes():
+    """mj_create validates shapes on the host; without a device it returns NULL
+    with a message (no crash)."""
+    from mjolnir_b200 import _lib
+
+    lib = _lib.load()
+    assert not lib.mj_create(0, 8, 3, 128, 16, 4, 1, _lib.MJ_KV_E2M3, 16, 2)  # h_q % h_k
+    assert b"invalid" in lib.mj_last_error()
+    assert not lib.mj_create(0, 64, 1, 128, 16, 4, 2, _lib.MJ_KV_E2M3, 16, 2)  # 128 rows per KV head
+    assert b"64 query rows" in lib.mj_last_error()

@@ -60,3 +60,21 @@ def test_pad_to_and_errors():
     assert len(p.work) == 64 and p.work[-1] == (0, 0, 0, 0)
     with pytest.raises(ValueError):
         plan_split_kv([300000] * 8, 2, 1, 148, ctas_per_sm=2, pad_to=3)
+
+
+def test_native_planner_matches_python():
+    """mj_plan_split_kv (C++, for hosts without Python) gives the same plans."""
+    import random
+
+    from mjolnir_b200 import _lib
+
+    rng = random.Random(1)
+    for _ in range(120):
+        n = rng.randint(1, 300)
+        lens = [rng.choice([rng.randint(0, 5000), rng.randint(1, 140000), 8192]) for _ in range(n)]
+        hk, nt = rng.choice([1, 2, 4, 8]), rng.choice([1, 2, 3])
+        sm, cps, ms = rng.choice([148, 132, 8]), rng.choice([1, 2]), rng.choice([1, 4, 16])
+        reb, ov, pad = rng.choice([True, False]), rng.choice([0.5, 2.0]), rng.choice([0, n * ms + 5])
+        p = plan_split_kv(lens, hk, nt, sm, ctas_per_sm=cps, max_splits=ms, pad_to=pad, rebalance=reb, item_overhead=ov)
+        w, ns, chunk = _lib.plan_split_kv(lens, hk, nt, sm, cps, ms, pad, reb, ov)
+        assert np.array_equal(w, p.work_array()) and ns == p.n_splits and chunk == p.chunk_tiles
