@@ -195,3 +195,77 @@ def expand_rows_e4m3(packed: np.ndarray, d: int, ratio=None) -> np.ndarray:
         h_k = packed.shape[-2]
         vals = (vals * _expand_scale(ratio, h_k, d)).astype(np.float32)
     return e4m3_bytes(vals)
+
+
+# ---------------------------------------------------------------------------
+# The other narrow formats of the reference's kernel harness (quant.py:14-47,
+# arch/thor/decode.py:108-115): e3m2 (6-bit, bias 3, max 28) and e2m1 (4-bit,
+# bias 1, max 6); same rounding rule as e2m3 (nearest, ties to the smaller
+# magnitude, saturating, no -0), 6-bit codes packed 4 per 3 bytes, 4-bit
+# codes 2 per byte, low nibble first (quant.py:50-65).
+# ---------------------------------------------------------------------------
+MINIFLOAT = {"e3m2": (3, 2, 3), "e2m3": (2, 3, 1), "e2m1": (2, 1, 1)}  # (exponent bits, mantissa bits, bias)
+BITS = {"e3m2": 6, "e2m3": 6, "e2m1": 4}
+
+
+def minifloat_table(fmt: str) -> np.ndarray:
+    """Value of every code of a narrow format (code = sign | exponent | mantissa)."""
+    eb, mb, bias = MINIFLOAT[fmt]
+    vals = []
+    for code in range(1 << (1 + eb + mb)):
+        sign = -1.0 if code >> (eb + mb) else 1.0
+        e = (code >> mb) & ((1 << eb) - 1)
+        m = code & ((1 << mb) - 1)
+        v = (m / (1 << mb)) * 2.0 ** (1 - bias) if e == 0 else (1 + m / (1 << mb)) * 2.0 ** (e - bias)
+        vals.append(sign * v)
+    return np.asarray(vals, dtype=np.float32)
+
+
+def minifloat_codes(x: np.ndarray, fmt: str) -> np.ndarray:
+    """float32 (already divided by the scale) -> uint8 codes of `fmt` (the
+    procedure of e2m3_codes on that format's table)."""
+    table = minifloat_table(fmt)
+    pos = table[: len(table) // 2]
+    half = len(pos)
+    x = np.asarray(x, dtype=np.float32)
+    ax = np.abs(x)
+    ax = np.where(ax > pos[-1], pos[-1], ax)
+    idx = np.searchsorted(pos, ax, side="left")
+    lo = np.clip(idx - 1, 0, half - 1)
+    hi = np.clip(idx, 0, half - 1)
+    with np.errstate(invalid="ignore"):
+        pick_lo = (ax - pos[lo]) <= (pos[hi] - ax)
+    mag = np.where(pick_lo, lo, hi).astype(np.int64)
+    neg = (x < 0) & (pos[mag] > 0)
+    return (mag + neg.astype(np.int64) * half).astype(np.uint8)
+
+
+def pack4(codes: np.ndarray) -> np.ndarray:
+    """(..., d) 4-bit codes -> (..., d/2) bytes, low nibble first."""
+    c = np.asarray(codes).astype(np.uint8)
+    d = c.shape[-1]
+    assert d % 2 == 0
+    c = c.reshape(*c.shape[:-1], d // 2, 2)
+    return (c[..., 0] | (c[..., 1] << 4)).astype(np.uint8)
+
+
+def unpack4(packed: np.ndarray, d: int) -> np.ndarray:
+    b = np.asarray(packed).astype(np.uint8)
+    codes = np.stack([b & 15, b >> 4], axis=-1)
+    return codes.reshape(*packed.shape[:-1], d).astype(np.uint8)
+
+
+def quantize_rows_narrow(x: np.ndarray, scale, fmt: str) -> np.ndarray:
+    """(..., h_k, d) float32 -> packed (..., h_k, d * bits / 8) bytes of `fmt`."""
+    x = np.asarray(x, dtype=np.float32)
+    h_k, d = x.shape[-2], x.shape[-1]
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        q = (x / _expand_scale(scale, h_k, d)).astype(np.float32)
+    codes = minifloat_codes(q, fmt)
+    return pack6(codes) if BITS[fmt] == 6 else pack4(codes)
+
+
+def decode_rows_narrow(packed: np.ndarray, d: int, fmt: str) -> np.ndarray:
+    """Packed rows of `fmt` -> code values (..., d) float32 (no scale)."""
+    codes = unpack6(packed, d) if BITS[fmt] == 6 else unpack4(packed, d)
+    return minifloat_table(fmt)[codes.astype(np.int64)]

@@ -81,6 +81,19 @@ def gen_quant(kvfp6):
     return out
 
 
+def gen_narrow(quant):
+    """e3m2 / e2m1 (and e2m3) codes of every bf16 value at three scales:
+    the reference's minifloat_quantize then pack_subbyte (quant.py:34-65)."""
+    out = {}
+    x = all_bf16().float().reshape(512, 1, 128)
+    for fmt, bits in (("e3m2", 6), ("e2m1", 4)):
+        for name, s in (("s1", 1.0), ("s037", 0.37), ("s3", 3.0)):
+            codes, _ = quant.minifloat_quantize(x / s, fmt)
+            out[f"{fmt}_all_{name}"] = quant.pack_subbyte(codes, bits).numpy()
+        out[f"{fmt}_table"] = quant.minifloat_table(fmt).numpy()
+    return out
+
+
 def make_pool(g, seq_lens, PS, h_k, d, kv_format, kvfp6, spare=3):
     """Shuffled pages; spare (unreferenced) pages poisoned (0x7F for fp8, 0xFF for e2m3)."""
     n_blocks = [max(1, math.ceil(L / PS)) for L in seq_lens]
@@ -195,14 +208,18 @@ def gen_plan(plan_split_kv):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MJOLNIR_REF_SRC", "/root/reference/src/mjolnir"))
+    ap.add_argument("--ref", default=os.environ.get("MJOLNIR_REF_SRC"),
+                    help="the reference package directory (src/mjolnir of its checkout)")
     args = ap.parse_args()
-    kvfp6, _quant, ref_decode, emulate_decode, plan_split_kv = _import_ref(args.ref)
+    if not args.ref:
+        ap.error("pass --ref or set MJOLNIR_REF_SRC")
+    kvfp6, quant, ref_decode, emulate_decode, plan_split_kv = _import_ref(args.ref)
     torch.manual_seed(0)
     np.savez_compressed(os.path.join(HERE, "quant.npz"), **gen_quant(kvfp6))
+    np.savez_compressed(os.path.join(HERE, "narrow.npz"), **gen_narrow(quant))
     np.savez_compressed(os.path.join(HERE, "decode.npz"), **gen_decode(kvfp6, ref_decode, emulate_decode))
     np.savez_compressed(os.path.join(HERE, "plan.npz"), **gen_plan(plan_split_kv))
-    for f in ("quant.npz", "decode.npz", "plan.npz"):
+    for f in ("quant.npz", "narrow.npz", "decode.npz", "plan.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

@@ -4,6 +4,7 @@ import math
 import os
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import attention, quant
@@ -128,3 +129,18 @@ def test_empty_causal_rows_are_zero():
     o, lse = attention.decode_attention(q, kv, kv, torch.tensor([[0, 1]]), [2], 1, 3, 0.1)
     assert (o[0] == 0).all() and torch.isinf(lse[0]).all()
     assert torch.isfinite(lse[1:]).all()
+
+
+@pytest.mark.parametrize("fmt", ["e3m2", "e2m1"])
+def test_narrow_formats_bit_exact_on_every_bf16(fmt):
+    """e3m2 and e2m1 (the reference harness's other narrow KV formats): the
+    oracle's table and quantizer equal the reference's on every bf16 value."""
+    g = np.load(os.path.join(GOLDEN, "narrow.npz"))
+    np.testing.assert_array_equal(quant.minifloat_table(fmt), g[f"{fmt}_table"])
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    x = quant.bf16_to_f32(bits).reshape(512, 1, 128)
+    for name, s in (("s1", 1.0), ("s037", 0.37), ("s3", 3.0)):
+        got = quant.quantize_rows_narrow(x, np.float32(s), fmt)
+        np.testing.assert_array_equal(got, g[f"{fmt}_all_{name}"], err_msg=f"{fmt} scale {s}")
+        d = quant.decode_rows_narrow(got, 128, fmt)
+        assert np.all(np.abs(d) <= quant.minifloat_table(fmt).max())
