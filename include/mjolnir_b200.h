@@ -59,9 +59,15 @@ extern "C" {
 #define MJ_DEV_BAD_SPLIT 2   /* work item split >= max_splits or seq >= part_seqs */
 #define MJ_DEV_TIMEOUT 3     /* a bounded wait in a pipelined kernel gave up */
 
-/* KV formats */
+/* KV formats. e2m3 / e3m2: 6-bit codes (sign | exponent | mantissa, biases
+ * 1 / 3, maxima 7.5 / 28, no inf or NaN) packed 4 per 3 bytes little-endian;
+ * e2m1: 4-bit codes (bias 1, max 6) packed 2 per byte, low nibble first
+ * (arch/thor/decode.py:108-115, quant.py:14-65). The vLLM path serves e4m3
+ * and e2m3; e3m2 and e2m1 are the reference harness's other formats. */
 #define MJ_KV_FP8_E4M3 0
 #define MJ_KV_E2M3 1
+#define MJ_KV_E3M2 2
+#define MJ_KV_E2M1 3
 
 /* element types of Q / O / new K,V rows */
 #define MJ_DT_BF16 0
@@ -85,7 +91,7 @@ extern "C" {
 const char* mj_last_error(void);
 /* MJ_ABI_VERSION of the loaded library. */
 int mj_abi_version(void);
-/* Bytes of one K (or V) row: head_size (fp8) or head_size*3/4 (e2m3); -1 if invalid. */
+/* Bytes of one K (or V) row: head_size (fp8), head_size*3/4 (e2m3, e3m2) or head_size/2 (e2m1); -1 if invalid. */
 int mj_row_bytes(int head_size, int kv_format);
 
 /* ------------------------------------------------------------------------ */

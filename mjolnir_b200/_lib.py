@@ -26,7 +26,9 @@ MJ_DEV_TIMEOUT = 3
 
 MJ_KV_FP8_E4M3 = 0
 MJ_KV_E2M3 = 1
-KV_FORMATS = {"fp8": MJ_KV_FP8_E4M3, "e2m3": MJ_KV_E2M3}
+MJ_KV_E3M2 = 2
+MJ_KV_E2M1 = 3
+KV_FORMATS = {"fp8": MJ_KV_FP8_E4M3, "e2m3": MJ_KV_E2M3, "e3m2": MJ_KV_E3M2, "e2m1": MJ_KV_E2M1}
 
 MJ_DT_BF16 = 0
 MJ_DT_FP16 = 1

@@ -5,7 +5,8 @@
 // The write is a few hundred KB per decode step and launch-latency bound, so
 // the kernel favours a single small launch over vector width.
 //
-// Semantics (bit-exact with the reference quantizers):
+// Semantics (bit-exact with the reference quantizers; e3m2 / e2m1 as e2m3 on
+// their own tables, 4-bit codes packed two per byte, low nibble first):
 //   e2m3: kvfp6.py:107-155 (_write_kv_kernel) / quant.py:34-65 -- x / s in fp32
 //         (IEEE division), round to nearest, ties to the smaller magnitude,
 //         saturate 7.5, no -0, little-endian 4-codes-in-3-bytes packing.
@@ -58,12 +59,17 @@ __global__ void __launch_bounds__(256) cache_write_kernel(mj_cache_write_args a)
         xin[i] = load_elem(src, base + c, a.src_dtype);
         x[i] = __fdiv_rn(xin[i], scale_of(sc, mode, h, c, d));
       }
-      if (FMT == MJ_KV_E2M3) {
-        uint32_t w = e2m3_code(x[0]) | (e2m3_code(x[1]) << 6) | (e2m3_code(x[2]) << 12) |
-                     (e2m3_code(x[3]) << 18);
+      if (FMT == MJ_KV_E2M3 || FMT == MJ_KV_E3M2) {
+        uint32_t c[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[i] = FMT == MJ_KV_E2M3 ? e2m3_code(x[i]) : e3m2_code(x[i]);
+        const uint32_t w = c[0] | (c[1] << 6) | (c[2] << 12) | (c[3] << 18);
         dst[3 * g + 0] = (uint8_t)(w & 0xFFu);
         dst[3 * g + 1] = (uint8_t)((w >> 8) & 0xFFu);
         dst[3 * g + 2] = (uint8_t)((w >> 16) & 0xFFu);
+      } else if (FMT == MJ_KV_E2M1) {
+        dst[2 * g + 0] = (uint8_t)(e2m1_code(x[0]) | (e2m1_code(x[1]) << 4));
+        dst[2 * g + 1] = (uint8_t)(e2m1_code(x[2]) | (e2m1_code(x[3]) << 4));
       } else {
         // A NaN input keeps its sign bit (0x7F / 0xFF) as the reference's host
         // division does; the device division returns a canonical NaN.
@@ -81,6 +87,10 @@ cudaError_t launch_cache_write(const mj_cache_write_args& a, cudaStream_t stream
   const unsigned blocks = (unsigned)((threads + 255) / 256);
   if (a.kv_format == MJ_KV_E2M3)
     cache_write_kernel<MJ_KV_E2M3><<<blocks, 256, 0, stream>>>(a);
+  else if (a.kv_format == MJ_KV_E3M2)
+    cache_write_kernel<MJ_KV_E3M2><<<blocks, 256, 0, stream>>>(a);
+  else if (a.kv_format == MJ_KV_E2M1)
+    cache_write_kernel<MJ_KV_E2M1><<<blocks, 256, 0, stream>>>(a);
   else
     cache_write_kernel<MJ_KV_FP8_E4M3><<<blocks, 256, 0, stream>>>(a);
   return cudaGetLastError();

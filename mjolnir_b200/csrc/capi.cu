@@ -49,7 +49,8 @@ int mj_abi_version(void) { return MJ_ABI_VERSION; }
 int mj_row_bytes(int head_size, int kv_format) {
   if (head_size <= 0 || head_size % 16) return -1;
   if (kv_format == MJ_KV_FP8_E4M3) return head_size;
-  if (kv_format == MJ_KV_E2M3) return head_size * 3 / 4;
+  if (kv_format == MJ_KV_E2M3 || kv_format == MJ_KV_E3M2) return head_size * 3 / 4;
+  if (kv_format == MJ_KV_E2M1) return head_size / 2;
   return -1;
 }
 
@@ -79,7 +80,7 @@ static int validate_decode(const mj_decode_args& a, const char* who) {
     return fail(MJ_ERR_INVALID, "%s: num_seqs %d q_len %d h_q %d h_k %d", who, a.num_seqs, a.q_len, a.h_q, a.h_k);
   if (a.head_size != 128 && a.head_size != 256)
     return fail(MJ_ERR_UNSUPPORTED, "%s: head_size %d (128 or 256)", who, a.head_size);
-  if (a.kv_format != MJ_KV_FP8_E4M3 && a.kv_format != MJ_KV_E2M3)
+  if (a.kv_format < MJ_KV_FP8_E4M3 || a.kv_format > MJ_KV_E2M1)
     return fail(MJ_ERR_INVALID, "%s: kv_format %d", who, a.kv_format);
   const int n_q = a.q_len * (a.h_q / a.h_k);
   if (n_q > 64) return fail(MJ_ERR_UNSUPPORTED, "%s: q_len * h_q / h_k = %d > 64 rows per KV head", who, n_q);

@@ -84,6 +84,64 @@ __device__ __forceinline__ uint32_t e2m3_code(float x) {
   return mag | neg;
 }
 
+// ---- e3m2 (bias 3, max 28) and e2m1 (bias 1, max 6) ------------------------
+// Values from the bit definitions; codes by the same rule as e2m3 (nearest,
+// ties to the smaller magnitude, saturating, NaN -> max, no -0). Above the
+// subnormal range the lower neighbour is the input truncated to the format's
+// mantissa bits and the step one unit of its last place.
+__device__ __forceinline__ float e3m2_value(uint32_t code) {
+  const uint32_t mag = code & 31u, e = mag >> 2, m = mag & 3u;
+  const uint32_t sixteenths = e ? ((4u + m) << (e - 1u)) : m;
+  const float v = (float)sixteenths * 0.0625f;
+  return (code & 32u) ? -v : v;
+}
+
+__device__ __forceinline__ float e2m1_value(uint32_t code) {
+  const uint32_t mag = code & 7u, e = mag >> 1, m = mag & 1u;
+  const uint32_t halves = e ? ((2u + m) << (e - 1u)) : m;
+  const float v = (float)halves * 0.5f;
+  return (code & 8u) ? -v : v;
+}
+
+// MB mantissa bits, BIAS, EB exponent bits; sub_step = the subnormal spacing.
+template <int EB, int MB, int BIAS>
+__device__ __forceinline__ uint32_t minifloat_code(float x) {
+  constexpr uint32_t kMagMax = (1u << (EB + MB)) - 1u;
+  constexpr float kMin = 1.0f / (float)(1u << (BIAS - 1));  // smallest normal: 2^(1 - BIAS)
+  const float vmax = (float)((2u << MB) - 1u) / (float)(1u << MB) * (float)(1u << ((1u << EB) - 1u - BIAS));
+  const float ax = fabsf(x);
+  uint32_t mag;
+  if (!(ax < vmax)) {  // >= max, +-inf or NaN
+    mag = kMagMax;
+  } else {
+    uint32_t lo;
+    float lo_v, step;
+    if (ax < kMin) {  // subnormals: spacing 2^(1 - BIAS - MB)
+      const float sub = kMin / (float)(1u << MB);
+      lo = (uint32_t)(ax / sub);
+      lo_v = (float)lo * sub;
+      step = sub;
+    } else {
+      const uint32_t u = __float_as_uint(ax);
+      const int E = (int)(u >> 23) - 127;
+      lo = ((uint32_t)(E + BIAS) << MB) | ((u >> (23 - MB)) & ((1u << MB) - 1u));
+      lo_v = __uint_as_float(u & ~((1u << (23 - MB)) - 1u));
+      step = __uint_as_float((uint32_t)(E - MB + 127) << 23);
+    }
+    if (ax == lo_v) {
+      mag = lo;
+    } else {
+      const float hi_v = lo_v + step;
+      mag = __fsub_rn(ax, lo_v) <= __fsub_rn(hi_v, ax) ? lo : lo + 1u;
+    }
+  }
+  const uint32_t neg = (x < 0.0f && mag) ? (1u << (EB + MB)) : 0u;  // NaN and -0 stay positive
+  return mag | neg;
+}
+
+__device__ __forceinline__ uint32_t e3m2_code(float x) { return minifloat_code<3, 2, 3>(x); }
+__device__ __forceinline__ uint32_t e2m1_code(float x) { return minifloat_code<2, 1, 1>(x); }
+
 // fp32 -> e4m3fn byte: round to nearest even, saturate at +-448, NaN keeps
 // its sign bit (0x7F / 0xFF).
 __device__ __forceinline__ uint8_t e4m3_byte(float x) {

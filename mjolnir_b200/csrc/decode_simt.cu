@@ -8,7 +8,7 @@
 // packing, quant.py:87-100), with an online softmax in base 2.
 //
 // Per 128-row tile: thread t dequantizes KV row t (K into registers for the
-// dot products, V into a half-precision SMEM tile -- exact for e4m3 and e2m3
+// dot products, V into a half-precision SMEM tile -- exact for every KV format
 // codes), the scores go through SMEM for the row-wise max / exp, and thread t
 // accumulates output column(s) t (+128) for every query row.
 //
@@ -40,6 +40,14 @@ __device__ __forceinline__ void load_codes16(const uint8_t* row, int c0, float* 
       out[4 * i + 2] = b.x;
       out[4 * i + 3] = b.y;
     }
+  } else if (FMT == MJ_KV_E2M1) {
+    // 16 codes = 8 bytes at byte offset c0 / 2 (8-byte aligned), low nibble first
+    const uint2 w = *reinterpret_cast<const uint2*>(row + (c0 >> 1));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      out[k] = e2m1_value((w.x >> (4 * k)) & 15u);
+      out[8 + k] = e2m1_value((w.y >> (4 * k)) & 15u);
+    }
   } else {
     // 16 codes = 12 bytes at byte offset c0 * 3 / 4 (4-byte aligned)
     const uint32_t* p = reinterpret_cast<const uint32_t*>(row + (c0 >> 2) * 3);
@@ -49,7 +57,10 @@ __device__ __forceinline__ void load_codes16(const uint8_t* row, int c0, float* 
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) out[4 * i + k] = e2m3_value((g[i] >> (6 * k)) & 63u);
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t code = (g[i] >> (6 * k)) & 63u;
+        out[4 * i + k] = FMT == MJ_KV_E2M3 ? e2m3_value(code) : e3m2_value(code);
+      }
     }
   }
 }
@@ -353,13 +364,19 @@ static cudaError_t launch_simt_nq(const mj_decode_args& a, int n_q, cudaStream_t
   return launch_simt_t<D, 64, FMT>(a, stream);
 }
 
+template <int D>
+static cudaError_t launch_simt_d(const mj_decode_args& a, int n_q, cudaStream_t stream) {
+  switch (a.kv_format) {
+    case MJ_KV_E2M3: return launch_simt_nq<D, MJ_KV_E2M3>(a, n_q, stream);
+    case MJ_KV_E3M2: return launch_simt_nq<D, MJ_KV_E3M2>(a, n_q, stream);
+    case MJ_KV_E2M1: return launch_simt_nq<D, MJ_KV_E2M1>(a, n_q, stream);
+    default: return launch_simt_nq<D, MJ_KV_FP8_E4M3>(a, n_q, stream);
+  }
+}
+
 cudaError_t launch_decode_simt(const mj_decode_args& a, cudaStream_t stream) {
   const int n_q = a.q_len * (a.h_q / a.h_k);
-  if (a.head_size == 128)
-    return a.kv_format == MJ_KV_E2M3 ? launch_simt_nq<128, MJ_KV_E2M3>(a, n_q, stream)
-                                     : launch_simt_nq<128, MJ_KV_FP8_E4M3>(a, n_q, stream);
-  return a.kv_format == MJ_KV_E2M3 ? launch_simt_nq<256, MJ_KV_E2M3>(a, n_q, stream)
-                                   : launch_simt_nq<256, MJ_KV_FP8_E4M3>(a, n_q, stream);
+  return a.head_size == 128 ? launch_simt_d<128>(a, n_q, stream) : launch_simt_d<256>(a, n_q, stream);
 }
 
 cudaError_t launch_combine(const mj_decode_args& a, cudaStream_t stream) {

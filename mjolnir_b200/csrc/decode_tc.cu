@@ -66,6 +66,58 @@ constexpr int kMergeMaxSplits = 16;
 // warp roles
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
+// Turn 16 e2m3 codes (12 packed bytes of a 16U6 slot) into 16 e4m3 bytes whose
+// values are the codes' values * 2^-6: sign moves from bit 5 to bit 7, the
+// 2-bit exponent and 3-bit mantissa stay (e4m3 bias 7 vs e2m3 bias 1).
+__device__ __forceinline__ uint32_t spread4(uint32_t g) {
+  uint32_t t = g + 15u * (g & 0xFFF000u);      // c2 c3 -> bits 16..27
+  t = t + 3u * (t & 0x0FC00FC0u);              // c1 -> byte 1, c3 -> byte 3
+  return t + 3u * (t & 0x20202020u);           // sign bit 5 -> bit 7 in every byte
+}
+
+__device__ __forceinline__ uint4 e2m3x16_to_e4m3(uint4 raw) {
+  const uint32_t g0 = raw.x & 0xFFFFFFu;
+  const uint32_t g1 = __funnelshift_r(raw.x, raw.y, 24) & 0xFFFFFFu;
+  const uint32_t g2 = __funnelshift_r(raw.y, raw.z, 16) & 0xFFFFFFu;
+  const uint32_t g3 = raw.z >> 8;
+  return make_uint4(spread4(g0), spread4(g1), spread4(g2), spread4(g3));
+}
+
+// e3m2: the same spread, then the 5 magnitude bits move up one place (e4m3
+// keeps the 3-bit exponent over bias 7 and gains a mantissa bit): value * 2^-4.
+__device__ __forceinline__ uint32_t e3m2_bytes(uint32_t t) { return ((t & 0x1F1F1F1Fu) << 1) | (t & 0x80808080u); }
+__device__ __forceinline__ uint4 e3m2x16_to_e4m3(uint4 raw) {
+  const uint4 t = e2m3x16_to_e4m3(raw);
+  return make_uint4(e3m2_bytes(t.x), e3m2_bytes(t.y), e3m2_bytes(t.z), e3m2_bytes(t.w));
+}
+
+// e2m1: a 16U4 slot holds 16 nibbles in its first 8 bytes; code s|e|m becomes
+// byte s<<7 | e<<3 | m<<2, value * 2^-6 (subnormals included).
+__device__ __forceinline__ uint32_t e2m1_bytes(uint32_t nib4) {  // 4 codes, one per byte (low nibbles)
+  return ((nib4 & 0x07070707u) << 2) | ((nib4 & 0x08080808u) << 4);
+}
+__device__ __forceinline__ uint4 e2m1x16_to_e4m3(uint4 raw) {
+  const uint32_t e0 = raw.x & 0x0F0F0F0Fu, o0 = (raw.x >> 4) & 0x0F0F0F0Fu;
+  const uint32_t e1 = raw.y & 0x0F0F0F0Fu, o1 = (raw.y >> 4) & 0x0F0F0F0Fu;
+  return make_uint4(e2m1_bytes(__byte_perm(e0, o0, 0x5140)), e2m1_bytes(__byte_perm(e0, o0, 0x7362)),
+                    e2m1_bytes(__byte_perm(e1, o1, 0x5140)), e2m1_bytes(__byte_perm(e1, o1, 0x7362)));
+}
+
+// Per-format constants of the tensor-core path.
+template <int FMT>
+struct Fmt {
+  static constexpr bool NARROW = FMT != MJ_KV_FP8_E4M3;  // V needs a conversion to e4m3
+  // kind::f8f6f4 operand format of K
+  static constexpr uint32_t MMA_FMT = FMT == MJ_KV_E2M3 ? 3u : FMT == MJ_KV_E3M2 ? 4u : FMT == MJ_KV_E2M1 ? 5u : 0u;
+  static constexpr uint32_t ROW = FMT == MJ_KV_E2M1 ? 64u : NARROW ? 96u : 128u;  // packed bytes per 128-code row
+  static constexpr float V_UNSCALE = FMT == MJ_KV_E3M2 ? 16.f : NARROW ? 64.f : 1.f;  // undoes the conversion's shift
+  static __device__ __forceinline__ uint4 convert(uint4 raw) {
+    if constexpr (FMT == MJ_KV_E3M2) return e3m2x16_to_e4m3(raw);
+    else if constexpr (FMT == MJ_KV_E2M1) return e2m1x16_to_e4m3(raw);
+    else return e2m3x16_to_e4m3(raw);
+  }
+};
+
 // warps 2-3 (and, with CVTW, a whole second warpgroup): V conversion (e2m3) /
 // tail zeroing (e4m3); then NWG softmax warpgroups of 4 warps
 
@@ -80,7 +132,7 @@ struct Cfg {
   static constexpr int THREADS = 128 * (1 + CVTW + NWG);
   static constexpr int CTAS_PER_SM = NWG == 1 ? 2 : 1;
   static constexpr int CVT_ROLE = 64 + 128 * CVTW;       // threads of the converter role
-  static constexpr bool SM_CONVERTS = FMT == MJ_KV_E2M3 && CVTW == 0;  // softmax warpgroups share the conversion
+  static constexpr bool SM_CONVERTS = Fmt<FMT>::NARROW && CVTW == 0;  // softmax warpgroups share the conversion
   static constexpr int CVT_THREADS = CVT_ROLE + (SM_CONVERTS ? 128 * NWG : 0);  // threads that convert a V tile
   // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
   // warpgroup w owns rows w * NQP .. of each block.
@@ -101,7 +153,7 @@ struct Cfg {
   static constexpr int REG_LO = NWG == 3 ? (CVTW ? 48 : 64) : CVTW ? 56 : 0;
   static constexpr int REG_HI = NWG == 3 ? (CVTW ? 128 : 144) : CVTW ? 128 : 0;
   static constexpr int REG_POOL = 128 * REG_LO * (1 + CVTW) + 128 * NWG * REG_HI;
-  static constexpr uint32_t K_TX = (FMT == MJ_KV_E2M3) ? 128u * 96u : 128u * 128u;  // bytes TMA reads per tile
+  static constexpr uint32_t K_TX = 128u * Fmt<FMT>::ROW;  // bytes TMA reads per tile operand
   // shared memory plan (offsets from the 1024-aligned dynamic shared memory base)
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + STAGES * kTileBytes;
@@ -121,22 +173,6 @@ struct Bars {
   uint64_t* drain;
 };
 
-// Turn 16 e2m3 codes (12 packed bytes of a 16U6 slot) into 16 e4m3 bytes whose
-// values are the codes' values * 2^-6: sign moves from bit 5 to bit 7, the
-// 2-bit exponent and 3-bit mantissa stay (e4m3 bias 7 vs e2m3 bias 1).
-__device__ __forceinline__ uint32_t spread4(uint32_t g) {
-  uint32_t t = g + 15u * (g & 0xFFF000u);      // c2 c3 -> bits 16..27
-  t = t + 3u * (t & 0x0FC00FC0u);              // c1 -> byte 1, c3 -> byte 3
-  return t + 3u * (t & 0x20202020u);           // sign bit 5 -> bit 7 in every byte
-}
-
-__device__ __forceinline__ uint4 e2m3x16_to_e4m3(uint4 raw) {
-  const uint32_t g0 = raw.x & 0xFFFFFFu;
-  const uint32_t g1 = __funnelshift_r(raw.x, raw.y, 24) & 0xFFFFFFu;
-  const uint32_t g2 = __funnelshift_r(raw.y, raw.z, 16) & 0xFFFFFFu;
-  const uint32_t g3 = raw.z >> 8;
-  return make_uint4(spread4(g0), spread4(g1), spread4(g2), spread4(g3));
-}
 
 // y0, y1 (|y| <= 448) -> three e4m3 terms each: y ~= hi + mid / 16 + lo / 256.
 // The residuals are exact in fp32 (hi is within a factor of 2 of y).
@@ -260,7 +296,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       mbar_init(&b.o_full[i], 1);
       if (i == 0) mbar_init(b.o_free, 128 * NWG);
       // e2m3: converter warps and softmax warpgroups share the V conversion
-      mbar_init(&b.v_ready[i], FMT == MJ_KV_E2M3 ? C::CVT_THREADS : C::CVT_ROLE);
+      mbar_init(&b.v_ready[i], Fmt<FMT>::NARROW ? C::CVT_THREADS : C::CVT_ROLE);
       mbar_init(&b.v_free[i], 1);
       mbar_init(&b.q_full[i], NWG);
     }
@@ -320,7 +356,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
              mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
         if (!ok) break;
-        if (FMT == MJ_KV_E2M3) {
+        if constexpr (Fmt<FMT>::NARROW) {
           // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
           // this role converts chunks ct, ct + CVT_THREADS, ...; without a
           // converter warpgroup the softmax warpgroups convert the others
@@ -329,9 +365,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
 #pragma unroll 2
           for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
             uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
-            *q = e2m3x16_to_e4m3(*q);
+            *q = Fmt<FMT>::convert(*q);
           }
-          // e2m3 has no NaN code: rows past the sequence end are finite and get P = 0
+          // narrow formats have no NaN code: rows past the sequence end are finite and get P = 0
         } else {
           // e4m3 rows past the sequence end inside its last page may hold NaN
           // bytes; NaN * 0 would poison O, so zero them (their P is 0)
@@ -419,7 +455,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
     } else if (warp == kWarpMma) {
       // ------------------------------------------------------------- MMA issuer
       if (lane == 0) {
-        const uint32_t idesc_s = idesc_f8f6f4(FMT == MJ_KV_E2M3 ? 3u : 0u, 0u, 0u, 0u, (uint32_t)NS);
+        const uint32_t idesc_s = idesc_f8f6f4(Fmt<FMT>::MMA_FMT, 0u, 0u, 0u, (uint32_t)NS);
         const uint32_t idesc_o = idesc_f8f6f4(0u, 0u, 1u, 1u, (uint32_t)NO);  // V and P both MN-major
         bool ok = true;
         int it = 0, jc = 0;
@@ -743,7 +779,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
 #pragma unroll 2
           for (int c = C::CVT_ROLE + sw * 128 + t; c < kTileBytes / 16; c += C::CVT_THREADS) {
             uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
-            *q = e2m3x16_to_e4m3(*q);
+            *q = Fmt<FMT>::convert(*q);
           }
           fence_proxy_async_smem();
           mbar_arrive(&b.v_ready[it & 1]);
@@ -780,7 +816,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         break;
       }
       const bool final_out = nsp <= 1;
-      const float vscale = (FMT == MJ_KV_E2M3 ? 64.f : 1.f) * vd / kPScale;
+      const float vscale = Fmt<FMT>::V_UNSCALE * vd / kPScale;
       const int qi0 = row0 / h_r, rr0 = row0 % h_r;
       auto qh_of = [&](int r) { return h * h_r + (rr0 + r) % h_r; };
       auto tok_of = [&](int r) { return (int64_t)seq * q_len + qi0 + (rr0 + r) / h_r; };
@@ -932,7 +968,7 @@ const char* tc_ineligible(const mj_decode_args& a) {
   if (a.head_size != 128) return "head_size != 128";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";
-  const uintptr_t al = a.kv_format == MJ_KV_E2M3 ? 32 : 16;
+  const uintptr_t al = a.kv_format == MJ_KV_FP8_E4M3 ? 16 : 32;
   if ((uintptr_t)a.k_cache % al || (uintptr_t)a.v_cache % al) return "KV view alignment";
   const int64_t st[6] = {a.k_stride_page, a.k_stride_row, a.k_stride_head, a.v_stride_page, a.v_stride_row, a.v_stride_head};
   for (int i = 0; i < 6; ++i)
@@ -942,17 +978,25 @@ const char* tc_ineligible(const mj_decode_args& a) {
   return nullptr;
 }
 
+// TMA element type of a KV format: 6-bit codes land 16 per 16-byte slot (12
+// packed bytes, 4 padding), 4-bit codes 16 per 16-byte slot (8 and 8).
+static CUtensorMapDataType tma_type(int kv_format) {
+  if (kv_format == MJ_KV_E2M3 || kv_format == MJ_KV_E3M2) return CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B;
+  if (kv_format == MJ_KV_E2M1) return CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;
+  return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+}
+
 static bool make_map(CUtensorMap* m, const void* base, int64_t s_page, int64_t s_row, int64_t s_head,
                      const mj_decode_args& a) {
-  const bool e2m3 = a.kv_format == MJ_KV_E2M3;
+  const bool narrow = a.kv_format != MJ_KV_FP8_E4M3;
   // a dimension of extent 1 never moves its coordinate; give it any legal stride
-  const int64_t fill = e2m3 ? 32 : 16;
+  const int64_t fill = narrow ? 32 : 16;
   cuuint64_t dims[4] = {128, (cuuint64_t)a.page_size, (cuuint64_t)a.h_k, (cuuint64_t)a.num_pages};
   cuuint64_t strides[3] = {(cuuint64_t)(s_row ? s_row : fill), (cuuint64_t)(s_head ? s_head : fill),
                            (cuuint64_t)(s_page ? s_page : fill)};
   cuuint32_t box[4] = {128, (cuuint32_t)a.page_size, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = encode_fn()(m, e2m3 ? CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+  CUresult r = encode_fn()(m, tma_type(a.kv_format), 4,
                            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -967,7 +1011,7 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t s_page, int64_t s
 // 5-D box -- (codes, 8 rows, K|V, row groups, page * h_k + head) -- loads a
 // page's K and V at once: half the TMA operations of separate boxes.
 static bool fused_layout(const mj_decode_args& a, int64_t* pagehead_stride) {
-  const int64_t rb = a.kv_format == MJ_KV_E2M3 ? 96 : 128;
+  const int64_t rb = mj_row_bytes(128, a.kv_format);
   if ((uintptr_t)a.v_cache != (uintptr_t)a.k_cache + (uintptr_t)rb) return false;
   if (a.k_stride_page != a.v_stride_page || a.k_stride_row != a.v_stride_row || a.k_stride_head != a.v_stride_head)
     return false;
@@ -982,15 +1026,14 @@ static bool fused_layout(const mj_decode_args& a, int64_t* pagehead_stride) {
 }
 
 static bool make_map_fused(CUtensorMap* m, const mj_decode_args& a, int64_t pagehead_stride) {
-  const bool e2m3 = a.kv_format == MJ_KV_E2M3;
-  const int64_t rb = e2m3 ? 96 : 128;
+  const int64_t rb = mj_row_bytes(128, a.kv_format);
   const int64_t heads = a.h_k > 1 ? a.h_k : 1;
   cuuint64_t dims[5] = {128, 8, 2, (cuuint64_t)(a.page_size / 8), (cuuint64_t)(a.num_pages * heads)};
   cuuint64_t strides[4] = {(cuuint64_t)a.k_stride_row, (cuuint64_t)rb, (cuuint64_t)(8 * a.k_stride_row),
                            (cuuint64_t)pagehead_stride};
   cuuint32_t box[5] = {128, 8, 2, (cuuint32_t)(a.page_size / 8), 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = encode_fn()(m, e2m3 ? CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 5,
+  CUresult r = encode_fn()(m, tma_type(a.kv_format), 5,
                            const_cast<void*>(a.k_cache), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1050,7 +1093,7 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
 template <int FMT, int NQP, bool FUSED>
 static cudaError_t launch_one_wg(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
                                  cudaStream_t stream) {
-  if constexpr (FMT == MJ_KV_E2M3) {
+  if constexpr (tc::Fmt<FMT>::NARROW) {
     cudaError_t e = launch_tc_t<FMT, NQP, 1, 1, FUSED>(a, mk, mv, stream);
     if (e != cudaErrorNotSupported) return e;
   }
@@ -1065,7 +1108,7 @@ static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensor
   if (n_q <= 16) return launch_one_wg<FMT, 16, FUSED>(a, mk, mv, stream);
   if (n_q <= 32) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
   cudaError_t e = cudaErrorNotSupported;
-  if constexpr (FMT == MJ_KV_E2M3) e = launch_tc_t<FMT, 16, 3, 1, FUSED>(a, mk, mv, stream);
+  if constexpr (tc::Fmt<FMT>::NARROW) e = launch_tc_t<FMT, 16, 3, 1, FUSED>(a, mk, mv, stream);
   if (e == cudaErrorNotSupported) e = launch_tc_t<FMT, 16, 3, 0, FUSED>(a, mk, mv, stream);
   if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
   return e;
@@ -1074,8 +1117,12 @@ static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensor
 template <bool FUSED>
 static cudaError_t dispatch_nq(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream) {
-  if (a.kv_format == MJ_KV_E2M3) return dispatch_fmt<MJ_KV_E2M3, FUSED>(a, n_q, mk, mv, stream);
-  return dispatch_fmt<MJ_KV_FP8_E4M3, FUSED>(a, n_q, mk, mv, stream);
+  switch (a.kv_format) {
+    case MJ_KV_E2M3: return dispatch_fmt<MJ_KV_E2M3, FUSED>(a, n_q, mk, mv, stream);
+    case MJ_KV_E3M2: return dispatch_fmt<MJ_KV_E3M2, FUSED>(a, n_q, mk, mv, stream);
+    case MJ_KV_E2M1: return dispatch_fmt<MJ_KV_E2M1, FUSED>(a, n_q, mk, mv, stream);
+    default: return dispatch_fmt<MJ_KV_FP8_E4M3, FUSED>(a, n_q, mk, mv, stream);
+  }
 }
 
 // Launch the tensor-core decode when it can run these arguments; *handled

@@ -127,7 +127,13 @@ def split_kv_cache(kv_cache: torch.Tensor, layout: str, row: int):
 def row_bytes(head_size: int, kv_format: str) -> int:
     if head_size % 16:
         raise ValueError(f"head_size {head_size} must be a multiple of 16")
-    return head_size if kv_format == "fp8" else head_size * 3 // 4
+    if kv_format == "fp8":
+        return head_size
+    if kv_format in ("e2m3", "e3m2"):
+        return head_size * 3 // 4
+    if kv_format == "e2m1":
+        return head_size // 2
+    raise ValueError(f"kv_format {kv_format!r}")
 
 
 _DT = {torch.bfloat16: _lib.MJ_DT_BF16, torch.float16: _lib.MJ_DT_FP16, torch.float32: _lib.MJ_DT_FP32}

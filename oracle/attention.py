@@ -37,6 +37,8 @@ def dequant_pool(pool_bytes: np.ndarray | torch.Tensor, kv_format: str, d: int) 
         return torch.from_numpy(quant.decode_fp8(b))
     if kv_format == "e2m3":
         return torch.from_numpy(quant.decode_rows_e2m3(b, d))
+    if kv_format in ("e3m2", "e2m1"):
+        return torch.from_numpy(quant.decode_rows_narrow(b, d, kv_format))
     raise ValueError(kv_format)
 
 

@@ -53,7 +53,10 @@ class Case:
             i += nb
         unused = perm[i:]
         self.block_table_cpu = bt
-        rb = self.row = d if kv_format == "fp8" else d * 3 // 4
+        from mjolnir_b200.runner import row_bytes
+
+        rb = self.row = row_bytes(d, kv_format)
+        vmax = {"e2m3": 7.5, "e3m2": 28.0, "e2m1": 6.0}.get(kv_format)
         # host pools: raw values -> quantized bytes (oracle) -> code values
         raw = {}
         for side in ("k", "v"):
@@ -74,9 +77,9 @@ class Case:
         if kv_format == "fp8":
             self.k_scale_w = self.v_scale_w = torch.ones(1)
         else:
-            # per (KV head, channel) amax / 7.5 (kvscales.e2m3_scales without headroom)
-            self.k_scale_w = raw["k"].abs().amax(dim=(0, 1)).clamp(min=1e-6) / 7.5
-            self.v_scale_w = raw["v"].abs().amax(dim=(0, 1)).clamp(min=1e-6) / 7.5
+            # per (KV head, channel) amax / the format's max (kvscales.e2m3_scales without headroom)
+            self.k_scale_w = raw["k"].abs().amax(dim=(0, 1)).clamp(min=1e-6) / vmax
+            self.v_scale_w = raw["v"].abs().amax(dim=(0, 1)).clamp(min=1e-6) / vmax
         self.bytes = {}
         self.vals = {}
         for side, sc in (("k", self.k_scale_w), ("v", self.v_scale_w)):
@@ -85,7 +88,7 @@ class Case:
                 by = quant.quantize_rows_fp8(xb, sc.numpy())
                 by[unused] = FP8_NAN
             else:
-                by = quant.quantize_rows_e2m3(xb, sc.numpy())
+                by = quant.quantize_rows_narrow(xb, sc.numpy(), kv_format)
                 by[unused] = E2M3_POISON
             self.bytes[side] = torch.from_numpy(by)
             self.vals[side] = attention.dequant_pool(by, kv_format, d)

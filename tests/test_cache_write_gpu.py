@@ -16,7 +16,9 @@ def _write(key, value, fmt, layout, num_pages, PS, slots, ks, vs):
     from mjolnir_b200.runner import split_kv_cache
 
     T, h_k, d = key.shape
-    rb = d if fmt == "fp8" else d * 3 // 4
+    from mjolnir_b200.runner import row_bytes
+
+    rb = row_bytes(d, fmt)
     cache = torch.full(LAYOUT_SHAPES[layout](num_pages, PS, h_k, rb), 0xA5, dtype=torch.uint8, device="cuda")
     kv, vv = split_kv_cache(cache, layout, rb)
     kvfp6.reshape_and_cache(key, value, kv, vv, slots.cuda(), ks.cuda(), vs.cuda(), fmt)
@@ -25,7 +27,7 @@ def _write(key, value, fmt, layout, num_pages, PS, slots, ks, vs):
 
 
 def _check(kv, vv, key, value, slots, ks, vs, fmt, PS):
-    qf = quant.quantize_rows_fp8 if fmt == "fp8" else quant.quantize_rows_e2m3
+    qf = quant.quantize_rows_fp8 if fmt == "fp8" else (lambda x, sc: quant.quantize_rows_narrow(x, sc, fmt))
     ref_k = qf(key.float().cpu().numpy(), ks.numpy())
     ref_v = qf(value.float().cpu().numpy(), vs.numpy())
     written = set()
@@ -42,7 +44,7 @@ def _check(kv, vv, key, value, slots, ks, vs, fmt, PS):
             assert (kv[blk, off] == 0xA5).all() and (vv[blk, off] == 0xA5).all(), "wrote a slot it was not given"
 
 
-@pytest.mark.parametrize("fmt", ["fp8", "e2m3"])
+@pytest.mark.parametrize("fmt", ["fp8", "e2m3", "e3m2", "e2m1"])
 @pytest.mark.parametrize("layout", ["BHN2D", "B2NHD", "2BHND"])
 def test_random_rows_all_scale_modes(fmt, layout):
     g = torch.Generator().manual_seed(11)
@@ -59,7 +61,7 @@ def test_random_rows_all_scale_modes(fmt, layout):
         _check(kv, vv, key, value, slots, ks, vs, fmt, PS)
 
 
-@pytest.mark.parametrize("fmt", ["fp8", "e2m3"])
+@pytest.mark.parametrize("fmt", ["fp8", "e2m3", "e3m2", "e2m1"])
 def test_every_bf16_value(fmt):
     """All 65536 bf16 bit patterns (NaN, inf, subnormals, ties) through the kernel."""
     bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
@@ -69,7 +71,7 @@ def test_every_bf16_value(fmt):
     for s in (1.0, 0.37, 3.0):
         sc = torch.tensor([s])
         kv, vv = _write(x.cuda(), x.cuda(), fmt, "BHN2D", 512 // PS, PS, slots, sc, sc)
-        qf = quant.quantize_rows_fp8 if fmt == "fp8" else quant.quantize_rows_e2m3
+        qf = quant.quantize_rows_fp8 if fmt == "fp8" else (lambda x, sc: quant.quantize_rows_narrow(x, sc, fmt))
         ref = qf(x.float().numpy(), np.array([s], np.float32))
         got = kv.reshape(512, 1, -1).numpy()
         bad = np.nonzero((got != ref).any(axis=-1))[0]

@@ -164,6 +164,22 @@ def test_tc_tensor_parallel_shards(kv_format, h_q, h_k):
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"tp shard {h_q}/{h_k}")
 
 
+@pytest.mark.parametrize("kv_format", ["e3m2", "e2m1"])
+@pytest.mark.parametrize("kernel", ["simt", "tc"])
+@pytest.mark.parametrize("q_len,h_q,page_size,layout", [(1, 8, 16, "BHN2D"), (1, 32, 64, "B2NHD"), (3, 16, 32, "BHN2D"),
+                                                        (6, 16, 16, "B2HND")])
+def test_other_narrow_formats(kv_format, kernel, q_len, h_q, page_size, layout):
+    """e3m2 and e2m1 caches (the reference harness's other narrow formats):
+    both kernels, one- and several-warpgroup variants, fused and separate
+    K / V boxes, with per-channel scales folded into Q and O."""
+    c = Case(seq_lens=(1500, q_len + 3, 777), q_len=q_len, h_q=h_q, h_k=2, page_size=page_size,
+             kv_format=kv_format, layout=layout, seed=81 + q_len)
+    out, _, _ = c.run(kernel=kernel)
+    ref, _ = c.oracle()
+    T = c.b * q_len
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"{kv_format} {kernel} q_len {q_len}")
+
+
 def test_tc_config4_shape_row_groups():
     """BASELINE config 4 shape (64 q / 8 KV heads, q_len 6 causal: 48 rows per KV
     head in 3 row groups), e2m3, shortened context."""
