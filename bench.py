@@ -1,6 +1,6 @@
 """Decode-attention benchmark (the BASELINE.json metric): KV GB/s and us/step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg5] [--kv fp8|e2m3]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg5] [--kv fp8|e2m3|e3m2|e2m1]
     python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
     python bench.py --impl reference ...   # the reference's CPU path (oracle port)
 
@@ -60,8 +60,11 @@ def seq_lens_for(w, seed=1234):
     return [int(w["L"])] * w["b"]
 
 
+VMAX = {"e2m3": 7.5, "e3m2": 28.0, "e2m1": 6.0}  # largest code value of each narrow format
+
+
 def row_bytes(d, kv):
-    return d if kv == "fp8" else d * 3 // 4
+    return {"fp8": d, "e2m3": d * 3 // 4, "e3m2": d * 3 // 4, "e2m1": d // 2}[kv]
 
 
 def kv_bytes(lens, h_k, d, kv):
@@ -113,15 +116,16 @@ class Workload:
                 x = torch.where(torch.rand(x.shape, generator=g, device=device) < outliers, x * 8, x)
             return x.to(torch.bfloat16)
 
-        # scales: fp8 per tensor 1.0; e2m3 per (KV head, channel) amax / 7.5 of a
-        # 1M-token sample of the same distribution (kvscales.e2m3_scales, no headroom)
+        # scales: fp8 per tensor 1.0; narrow formats per (KV head, channel) amax / the
+        # format's max of a 1M-token sample of the same distribution (kvscales.e2m3_scales,
+        # no headroom)
         if self.fmt == "fp8":
             self.k_scale = self.v_scale = torch.ones(1, device=device)
         else:
             smp = gen(1 << 20).float()
-            self.k_scale = (smp.abs().amax(0).clamp(min=1e-6) / 7.5).contiguous()
+            self.k_scale = (smp.abs().amax(0).clamp(min=1e-6) / VMAX[self.fmt]).contiguous()
             smp = gen(1 << 20).float()
-            self.v_scale = (smp.abs().amax(0).clamp(min=1e-6) / 7.5).contiguous()
+            self.v_scale = (smp.abs().amax(0).clamp(min=1e-6) / VMAX[self.fmt]).contiguous()
             del smp
         chunk = 1 << 19  # tokens per fill step
         total = self.num_pages * PS
@@ -131,7 +135,7 @@ class Workload:
             kvfp6.reshape_and_cache(gen(n), gen(n), self.k_view, self.v_view, slots, self.k_scale, self.v_scale, self.fmt)
         torch.cuda.synchronize(device)
         h_r = self.h_q // self.h_k
-        if self.fmt == "e2m3":
+        if self.fmt != "fp8":
             self.q_mul = self.k_scale.repeat_interleave(h_r, 0).contiguous()
             self.o_mul = self.v_scale.repeat_interleave(h_r, 0).contiguous()
             self.kd = self.vd = torch.ones(1, device=device)
@@ -342,7 +346,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
-    ap.add_argument("--kv", default=None, choices=[None, "fp8", "e2m3"])
+    ap.add_argument("--kv", default=None, choices=[None, "fp8", "e2m3", "e3m2", "e2m1"])
     ap.add_argument("--page-size", type=int, default=None, help="override the workload's KV page size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -486,7 +490,7 @@ def main():
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "fp8-e4m3 KV" if wl.fmt == "fp8" else "e2m3 KV",
+        "dtype": "fp8-e4m3 KV" if wl.fmt == "fp8" else f"{wl.fmt} KV",
         "data": "synthetic (N(0,1) K/V quantized by the repo's write kernel, shuffled pages, random Q)",
         "config": {"workload": args.workload, "kv_format": wl.fmt, "batch": wl.b, "h_q": WORKLOADS[args.workload]["h_q"],
                    "h_k": WORKLOADS[args.workload]["h_k"], "head_dim": wl.d, "q_len": wl.q_len,

@@ -46,7 +46,7 @@ def _sampled_reference(wl, seqs, heads):
 
 
 @pytest.mark.parametrize("workload,kv", [("cfg2", "fp8"), ("cfg3", "e2m3"), ("ns", "e2m3"), ("cfg4", "e2m3"),
-                                         ("cfg5", "e2m3"), ("cfg5", "fp8")])
+                                         ("cfg5", "e2m3"), ("cfg5", "fp8"), ("ns", "e3m2"), ("ns", "e2m1")])
 def test_full_size_step_sampled_parity(workload, kv):
     import bench
 
