@@ -24,6 +24,7 @@ __device__ __forceinline__ float scale_of(const float* s, int mode, int h, int c
 
 template <int FMT>
 __global__ void __launch_bounds__(256) cache_write_kernel(mj_cache_write_args a) {
+  griddep_wait();  // the new rows come from the previous kernel (PDL launch)
   const int warp = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   const int64_t pair = warp;
@@ -85,15 +86,14 @@ cudaError_t launch_cache_write(const mj_cache_write_args& a, cudaStream_t stream
   const int64_t pairs = a.num_tokens * a.h_k;
   const int64_t threads = pairs * 32;
   const unsigned blocks = (unsigned)((threads + 255) / 256);
-  if (a.kv_format == MJ_KV_E2M3)
-    cache_write_kernel<MJ_KV_E2M3><<<blocks, 256, 0, stream>>>(a);
-  else if (a.kv_format == MJ_KV_E3M2)
-    cache_write_kernel<MJ_KV_E3M2><<<blocks, 256, 0, stream>>>(a);
-  else if (a.kv_format == MJ_KV_E2M1)
-    cache_write_kernel<MJ_KV_E2M1><<<blocks, 256, 0, stream>>>(a);
-  else
-    cache_write_kernel<MJ_KV_FP8_E4M3><<<blocks, 256, 0, stream>>>(a);
-  return cudaGetLastError();
+  // No early trigger: the decode that follows may start only after every
+  // CTA of this write has exited, so no CTA of an earlier kernel still waits
+  // for resources (shared memory, TMEM) that a starting decode would hold.
+  auto kern = cache_write_kernel<MJ_KV_FP8_E4M3>;
+  if (a.kv_format == MJ_KV_E2M3) kern = cache_write_kernel<MJ_KV_E2M3>;
+  else if (a.kv_format == MJ_KV_E3M2) kern = cache_write_kernel<MJ_KV_E3M2>;
+  else if (a.kv_format == MJ_KV_E2M1) kern = cache_write_kernel<MJ_KV_E2M1>;
+  return launch_kernel(kern, dim3(blocks), dim3(256), 0, stream, a);
 }
 
 }  // namespace mj

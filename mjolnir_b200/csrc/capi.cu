@@ -3,6 +3,7 @@
 // the last failure of the calling thread is available from mj_last_error().
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -38,6 +39,14 @@ static bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p % a) == 0
 namespace mj {
 // Lets other translation units of the library report through mj_last_error().
 int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("MJOLNIR_PDL");
+    return !(v && v[0] == '0' && v[1] == 0);
+  }();
+  return on;
+}
 }  // namespace mj
 
 extern "C" {

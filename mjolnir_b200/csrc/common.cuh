@@ -163,4 +163,32 @@ __device__ __forceinline__ float descale_at(const float* p, int mode, int seq, i
   return p[(int64_t)seq * h_k + h];
 }
 
+// ---- programmatic dependent launch (PDL) -----------------------------------
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still draining; every thread that reads
+// memory the previous kernel wrote first waits here for that grid to complete
+// and flush (a no-op for a kernel launched without the attribute).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next PDL-launched kernel be scheduled once every CTA of this grid
+// has issued it (or exited); its own griddep_wait still waits for this grid.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialization unless MJOLNIR_PDL=0.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace mj

@@ -79,6 +79,8 @@ template <int D, int NQ, int FMT>
 __global__ void __launch_bounds__(128) decode_simt_kernel(const mj_decode_args a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   SimtSmem<D, NQ>& sm = *reinterpret_cast<SimtSmem<D, NQ>*>(smem_raw);
+  griddep_wait();  // the cache write before it (PDL launch)
+  if (a.with_combine) griddep_launch_dependents();  // the combine may queue up behind this grid
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int4 wi = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
   const int seq = wi.x, tb = wi.y, te = wi.z, split = wi.w;
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(const mj_decode_args a
 // m = max_j lse_j, w_j = exp(lse_j - m), O = sum_j w_j O_j / sum_j w_j,
 // lse = m + log(sum_j w_j). Sequences with n_splits <= 1 were written final.
 __global__ void __launch_bounds__(128) combine_kernel(const mj_decode_args a) {
+  griddep_wait();  // the partials of the decode before it (PDL launch)
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int h_k = a.h_k, h_r = a.h_q / a.h_k, q_len = a.q_len, n_q = q_len * h_r, D = a.head_size;
@@ -352,8 +355,7 @@ static cudaError_t launch_simt_t(const mj_decode_args& a, cudaStream_t stream) {
     attr_done = true;
   }
   dim3 grid((unsigned)a.num_work, (unsigned)a.h_k);
-  decode_simt_kernel<D, NQ, FMT><<<grid, 128, smem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_kernel(decode_simt_kernel<D, NQ, FMT>, grid, dim3(128), smem, stream, a);
 }
 
 template <int D, int FMT>
@@ -384,8 +386,7 @@ cudaError_t launch_combine(const mj_decode_args& a, cudaStream_t stream) {
   const int64_t warps = (int64_t)a.num_seqs * a.h_k * n_q;
   if (warps == 0) return cudaSuccess;
   const unsigned blocks = (unsigned)((warps * 32 + 127) / 128);
-  combine_kernel<<<blocks, 128, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_kernel(combine_kernel, dim3(blocks), dim3(128), 0, stream, a);
 }
 
 }  // namespace mj

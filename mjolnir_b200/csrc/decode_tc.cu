@@ -309,6 +309,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
     prefetch_tmap(&tmk);
     prefetch_tmap(&tmv);
   }
+  // PDL: wait for the cache write before it before any global read, and
+  // before taking TMEM, so a waiting CTA holds no tensor memory.
+  griddep_wait();
   if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
@@ -317,6 +320,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;  // S0 [0,NS) S1 [NS,2NS) O [2NS,2NS+NO)
+  // Every CTA is resident and holds its TMEM: the combine launch behind this
+  // grid (no TMEM, no shared memory) may be scheduled and wait on the GPU.
+  if (a.with_combine) griddep_launch_dependents();
 
   constexpr uint32_t ATOM = FUSED ? 2048u : 1024u;  // byte stride between 8-row swizzle atoms of K (or V)
   auto kbuf = [&](int st) { return FUSED ? sm + st * 2 * kTileBytes : sm + C::K_OFF + st * kTileBytes; };
@@ -964,7 +970,6 @@ static EncodeTiledFn encode_fn() {
 
 // Why the tensor-core kernel cannot run these arguments (nullptr = it can).
 const char* tc_ineligible(const mj_decode_args& a) {
-  const int n_q = a.q_len * (a.h_q / a.h_k);
   if (a.head_size != 128) return "head_size != 128";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";
@@ -1081,8 +1086,7 @@ static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, c
   const int n_q = a.q_len * (a.h_q / a.h_k);
   const int64_t jobs = (int64_t)a.num_work * a.h_k * ((n_q + C::RT - 1) / C::RT);
   const unsigned grid = (unsigned)(jobs < slots ? jobs : slots);
-  kern<<<grid, C::THREADS, smem, stream>>>(a, mk, mv);
-  return cudaGetLastError();
+  return launch_kernel(kern, dim3(grid), dim3(C::THREADS), (size_t)smem, stream, a, mk, mv);
 }
 
 // Variant by query rows per KV head (n_q): one warpgroup of 4, 8 or 16 rows
