@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define MJ_ABI_VERSION 2
+#define MJ_ABI_VERSION 3
 
 /* status codes */
 #define MJ_OK 0
@@ -62,12 +62,18 @@ extern "C" {
 /* KV formats. e2m3 / e3m2: 6-bit codes (sign | exponent | mantissa, biases
  * 1 / 3, maxima 7.5 / 28, no inf or NaN) packed 4 per 3 bytes little-endian;
  * e2m1: 4-bit codes (bias 1, max 6) packed 2 per byte, low nibble first
- * (arch/thor/decode.py:108-115, quant.py:14-65). The vLLM path serves e4m3
- * and e2m3; e3m2 and e2m1 are the reference harness's other formats. */
+ * (arch/thor/decode.py:108-115, quant.py:14-65). nvfp4: e2m1 codes as e2m1
+ * plus one e4m3 scale byte per 16 elements of a row in a separate scale
+ * tensor (logical (num_pages, page_size, h_k, head_size / 16) bytes) and a
+ * global fp32 scale gs; the value multiplied is e4m3(code * scale * 2^-3)
+ * with descale gs * 2^3 (quant.py:68-84, arch/thor/decode.py:980-1030).
+ * The vLLM path serves e4m3 and e2m3; the others are the reference
+ * harness's formats. */
 #define MJ_KV_FP8_E4M3 0
 #define MJ_KV_E2M3 1
 #define MJ_KV_E3M2 2
 #define MJ_KV_E2M1 3
+#define MJ_KV_NVFP4 4
 
 /* element types of Q / O / new K,V rows */
 #define MJ_DT_BF16 0
@@ -91,7 +97,7 @@ extern "C" {
 const char* mj_last_error(void);
 /* MJ_ABI_VERSION of the loaded library. */
 int mj_abi_version(void);
-/* Bytes of one K (or V) row: head_size (fp8), head_size*3/4 (e2m3, e3m2) or head_size/2 (e2m1); -1 if invalid. */
+/* Bytes of one K (or V) row: head_size (fp8), head_size*3/4 (e2m3, e3m2) or head_size/2 (e2m1, nvfp4 codes); -1 if invalid. */
 int mj_row_bytes(int head_size, int kv_format);
 
 /* ------------------------------------------------------------------------ */
@@ -103,6 +109,10 @@ int mj_row_bytes(int head_size, int kv_format);
 /* the smaller magnitude, saturate at 7.5, no -0; codes packed little-endian */
 /* (c0 | c1<<6 | c2<<12 | c3<<18 -> 3 bytes) -- quant.py:34-65.              */
 /* fp8: x / scale in fp32, round to nearest even, saturate at +-448.         */
+/* nvfp4 (quant.py:68-84 with a given global scale gs = k_scale / v_scale,  */
+/* per tensor or per KV head): per group of 16 elements the scale byte      */
+/* e4m3(min(amax / 6 / gs, 448)), then each code e2m1(x / (scale * gs)),    */
+/* 0 where that product is 0; head_size a multiple of 128.                  */
 typedef struct mj_cache_write_args {
   const void* key;              /* (num_tokens, h_k, head_size), head dim contiguous */
   const void* value;
@@ -118,13 +128,18 @@ typedef struct mj_cache_write_args {
   int64_t v_stride_page, v_stride_row, v_stride_head; /* bytes */
   int64_t num_pages;
   int page_size;
-  int kv_format;                /* MJ_KV_FP8_E4M3 | MJ_KV_E2M3 */
+  int kv_format;                /* MJ_KV_* */
   const int64_t* slot_mapping;  /* (num_tokens,) */
   const float* k_scale;         /* per k_scale_mode */
   int k_scale_mode;             /* MJ_SCALE_TENSOR | _HEAD | _CHANNEL */
   const float* v_scale;
   int v_scale_mode;
   int32_t* status;              /* optional device status word (MJ_DEV_*) */
+  /* nvfp4 only: the group scale tensors, logical (num_pages, page_size, h_k, head_size / 16) bytes */
+  void* k_scales;
+  void* v_scales;
+  int64_t ks_stride_page, ks_stride_row, ks_stride_head; /* bytes */
+  int64_t vs_stride_page, vs_stride_row, vs_stride_head; /* bytes */
 } mj_cache_write_args;
 
 int mj_cache_write(const mj_cache_write_args* args, void* stream);
@@ -175,6 +190,13 @@ typedef struct mj_decode_args {
    * others, and the CUDA-core kernel, ignore the counters. Replaces the reference's planned last-CTA merge
    * (arch/thor/decode.py:1417-1469, plan.py:122-129). */
   int32_t* merge_counters;
+  /* nvfp4 only: the group scale tensors, logical (num_pages, page_size, h_k,
+   * head_size / 16) bytes, rows 8-byte aligned for the tensor-core kernel;
+   * k_descale / v_descale carry gs * 2^3 (arch/thor/call.py:138-139, :343-356) */
+  const void* k_scales;
+  const void* v_scales;
+  int64_t ks_stride_page, ks_stride_row, ks_stride_head; /* bytes */
+  int64_t vs_stride_page, vs_stride_row, vs_stride_head; /* bytes */
 } mj_decode_args;
 
 int mj_decode(const mj_decode_args* args, void* stream);
@@ -224,17 +246,19 @@ int mj_runner_status(mj_runner* runner);
 void mj_destroy(mj_runner* runner);
 
 /* ------------------------------------------------------------------------ */
-/* e2m3 -> e4m3 page expansion for steps a stock fallback backend runs on an */
-/* e2m3 cache. Replaces kvfp6.py:257-335 `expand_pages_to_fp8` (called from  */
-/* backend.py:573-607 on the page map of builder.py:479-509). Output page j  */
-/* (0 <= j < num_out_pages) receives the K and V rows of cache page          */
+/* Narrow -> e4m3 page expansion for steps a stock fallback backend runs on */
+/* a narrow cache. Replaces kvfp6.py:257-335 `expand_pages_to_fp8` (called   */
+/* from backend.py:573-607 on the page map of builder.py:479-509). Output    */
+/* page j (0 <= j < num_out_pages) receives the K and V rows of cache page   */
 /* src_pages[j]: each e4m3 byte = e4m3(code_value * ratio) with the fp32      */
 /* product rounded to nearest even and saturated at +-448 (ratio = 1 when    */
-/* the pointer is null, which gives the e2m3 values exactly). A src page     */
-/* outside [0, num_pages) flags MJ_DEV_BAD_PAGE and its output page is left  */
-/* untouched. Alignment: packed rows 4-byte aligned, output rows 16-byte.    */
+/* the pointer is null, which gives e2m3 / e2m1 values exactly). nvfp4: the */
+/* code value is e4m3(code * scale * 2^-3), the value its tensor-core MMA    */
+/* reads, then times the ratio as above. A src page outside [0, num_pages)  */
+/* flags MJ_DEV_BAD_PAGE and its output page is left untouched. Alignment:  */
+/* packed rows 4-byte aligned, output rows 16-byte.                          */
 typedef struct mj_expand_args {
-  const void* k_cache;          /* e2m3 logical (num_pages, page_size, h_k, row_bytes) */
+  const void* k_cache;          /* narrow logical (num_pages, page_size, h_k, row_bytes) */
   const void* v_cache;
   int64_t k_stride_page, k_stride_row, k_stride_head; /* bytes */
   int64_t v_stride_page, v_stride_row, v_stride_head; /* bytes */
@@ -251,6 +275,11 @@ typedef struct mj_expand_args {
   const float* v_ratio;
   int v_ratio_mode;
   int32_t* status;              /* optional device status word (MJ_DEV_*) */
+  int kv_format;                /* MJ_KV_E2M3 | _E3M2 | _E2M1 | _NVFP4 */
+  const void* k_scales;         /* nvfp4 only: (num_pages, page_size, h_k, head_size / 16) bytes */
+  const void* v_scales;
+  int64_t ks_stride_page, ks_stride_row, ks_stride_head; /* bytes */
+  int64_t vs_stride_page, vs_stride_row, vs_stride_head; /* bytes */
 } mj_expand_args;
 
 int mj_expand_pages(const mj_expand_args* args, void* stream);

@@ -28,7 +28,9 @@ MJ_KV_FP8_E4M3 = 0
 MJ_KV_E2M3 = 1
 MJ_KV_E3M2 = 2
 MJ_KV_E2M1 = 3
-KV_FORMATS = {"fp8": MJ_KV_FP8_E4M3, "e2m3": MJ_KV_E2M3, "e3m2": MJ_KV_E3M2, "e2m1": MJ_KV_E2M1}
+MJ_KV_NVFP4 = 4
+KV_FORMATS = {"fp8": MJ_KV_FP8_E4M3, "e2m3": MJ_KV_E2M3, "e3m2": MJ_KV_E3M2, "e2m1": MJ_KV_E2M1,
+              "nvfp4": MJ_KV_NVFP4}
 
 MJ_DT_BF16 = 0
 MJ_DT_FP16 = 1
@@ -65,6 +67,9 @@ class CacheWriteArgs(C.Structure):
         ("k_scale", _vp), ("k_scale_mode", _i32),
         ("v_scale", _vp), ("v_scale_mode", _i32),
         ("status", _vp),
+        ("k_scales", _vp), ("v_scales", _vp),
+        ("ks_stride_page", _i64), ("ks_stride_row", _i64), ("ks_stride_head", _i64),
+        ("vs_stride_page", _i64), ("vs_stride_row", _i64), ("vs_stride_head", _i64),
     ]
 
 
@@ -82,6 +87,10 @@ class ExpandArgs(C.Structure):
         ("k_ratio", _vp), ("k_ratio_mode", _i32),
         ("v_ratio", _vp), ("v_ratio_mode", _i32),
         ("status", _vp),
+        ("kv_format", _i32),
+        ("k_scales", _vp), ("v_scales", _vp),
+        ("ks_stride_page", _i64), ("ks_stride_row", _i64), ("ks_stride_head", _i64),
+        ("vs_stride_page", _i64), ("vs_stride_row", _i64), ("vs_stride_head", _i64),
     ]
 
 
@@ -108,6 +117,9 @@ class DecodeArgs(C.Structure):
         ("kernel", _i32),
         ("status", _vp),
         ("merge_counters", _vp),
+        ("k_scales", _vp), ("v_scales", _vp),
+        ("ks_stride_page", _i64), ("ks_stride_row", _i64), ("ks_stride_head", _i64),
+        ("vs_stride_page", _i64), ("vs_stride_row", _i64), ("vs_stride_head", _i64),
     ]
 
 

@@ -12,6 +12,9 @@
 //         saturate 7.5, no -0, little-endian 4-codes-in-3-bytes packing.
 //   fp8 : (x / s) -> e4m3 round-to-nearest-even, saturating at +-448
 //         (arch/thor/harness.py:588-590 plus vLLM's saturating write).
+//   nvfp4: quant.py:68-84 with the global scale given (s = gs): per 16
+//         elements sc = e4m3(min(amax / 6 / gs, 448)), codes e2m1(x / (sc * gs))
+//         (0 where sc * gs is 0), scale bytes into the separate scale tensor.
 #include "common.cuh"
 
 namespace mj {
@@ -58,9 +61,32 @@ __global__ void __launch_bounds__(256) cache_write_kernel(mj_cache_write_args a)
       for (int i = 0; i < 4; ++i) {
         const int c = 4 * g + i;
         xin[i] = load_elem(src, base + c, a.src_dtype);
-        x[i] = __fdiv_rn(xin[i], scale_of(sc, mode, h, c, d));
+        if (FMT != MJ_KV_NVFP4) x[i] = __fdiv_rn(xin[i], scale_of(sc, mode, h, c, d));
       }
-      if (FMT == MJ_KV_E2M3 || FMT == MJ_KV_E3M2) {
+      if (FMT == MJ_KV_NVFP4) {
+        // a 16-element scale group is 4 consecutive lanes (head_size % 128 == 0,
+        // so every lane of the warp takes part in each pass)
+        float am = nan_max(nan_max(fabsf(xin[0]), fabsf(xin[1])), nan_max(fabsf(xin[2]), fabsf(xin[3])));
+        am = nan_max(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = nan_max(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        const float gs = scale_of(sc, mode, h, 0, d);
+        float s = __fdiv_rn(__fdiv_rn(am, 6.0f), gs);
+        s = s > 448.f ? 448.f : s;  // NaN stays NaN
+        const uint8_t sb = e4m3_byte(s);
+        const float den = e4m3_value(sb) * gs;
+        uint32_t c[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[i] = e2m1_code(den > 0.f ? __fdiv_rn(xin[i], fmaxf(den, 1e-30f)) : 0.f);
+        dst[2 * g + 0] = (uint8_t)(c[0] | (c[1] << 4));
+        dst[2 * g + 1] = (uint8_t)(c[2] | (c[3] << 4));
+        if ((g & 3) == 0) {
+          uint8_t* sdst = (uint8_t*)(side ? a.v_scales : a.k_scales) +
+                          page * (side ? a.vs_stride_page : a.ks_stride_page) +
+                          row * (side ? a.vs_stride_row : a.ks_stride_row) +
+                          h * (side ? a.vs_stride_head : a.ks_stride_head);
+          sdst[g >> 2] = sb;
+        }
+      } else if (FMT == MJ_KV_E2M3 || FMT == MJ_KV_E3M2) {
         uint32_t c[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) c[i] = FMT == MJ_KV_E2M3 ? e2m3_code(x[i]) : e3m2_code(x[i]);
@@ -90,7 +116,8 @@ cudaError_t launch_cache_write(const mj_cache_write_args& a, cudaStream_t stream
   // CTA of this write has exited, so no CTA of an earlier kernel still waits
   // for resources (shared memory, TMEM) that a starting decode would hold.
   auto kern = cache_write_kernel<MJ_KV_FP8_E4M3>;
-  if (a.kv_format == MJ_KV_E2M3) kern = cache_write_kernel<MJ_KV_E2M3>;
+  if (a.kv_format == MJ_KV_NVFP4) kern = cache_write_kernel<MJ_KV_NVFP4>;
+  else if (a.kv_format == MJ_KV_E2M3) kern = cache_write_kernel<MJ_KV_E2M3>;
   else if (a.kv_format == MJ_KV_E3M2) kern = cache_write_kernel<MJ_KV_E3M2>;
   else if (a.kv_format == MJ_KV_E2M1) kern = cache_write_kernel<MJ_KV_E2M1>;
   return launch_kernel(kern, dim3(blocks), dim3(256), 0, stream, a);

@@ -59,8 +59,20 @@ int mj_row_bytes(int head_size, int kv_format) {
   if (head_size <= 0 || head_size % 16) return -1;
   if (kv_format == MJ_KV_FP8_E4M3) return head_size;
   if (kv_format == MJ_KV_E2M3 || kv_format == MJ_KV_E3M2) return head_size * 3 / 4;
-  if (kv_format == MJ_KV_E2M1) return head_size / 2;
+  if (kv_format == MJ_KV_E2M1 || kv_format == MJ_KV_NVFP4) return head_size / 2;
   return -1;
+}
+
+// nvfp4 scale tensors: present, and (for the tensor-core kernel's 8-byte
+// copies) with 8-byte aligned rows when `align8`.
+static const char* nvfp4_scales_problem(const void* ks, const void* vs, const int64_t* strides, bool align8) {
+  if (!ks || !vs) return "nvfp4 needs k_scales and v_scales";
+  if (align8) {
+    if (!aligned(ks, 8) || !aligned(vs, 8)) return "nvfp4 scale rows must be 8-byte aligned";
+    for (int i = 0; i < 6; ++i)
+      if (strides[i] % 8) return "nvfp4 scale strides must be multiples of 8 bytes";
+  }
+  return nullptr;
 }
 
 int mj_cache_write(const mj_cache_write_args* args, void* stream) {
@@ -81,6 +93,14 @@ int mj_cache_write(const mj_cache_write_args* args, void* stream) {
     if (m != MJ_SCALE_TENSOR && m != MJ_SCALE_HEAD && m != MJ_SCALE_CHANNEL)
       return fail(MJ_ERR_INVALID, "mj_cache_write: scale mode %d", m);
   if (a.num_tokens * a.h_k > (int64_t)INT32_MAX / 32) return fail(MJ_ERR_UNSUPPORTED, "mj_cache_write: too many rows");
+  if (a.kv_format == MJ_KV_NVFP4) {
+    if (a.head_size % 128) return fail(MJ_ERR_UNSUPPORTED, "mj_cache_write: nvfp4 head_size %d (a multiple of 128)", a.head_size);
+    if (a.k_scale_mode == MJ_SCALE_CHANNEL || a.v_scale_mode == MJ_SCALE_CHANNEL)
+      return fail(MJ_ERR_INVALID, "mj_cache_write: the nvfp4 global scale is per tensor or per KV head");
+    const int64_t st[6] = {a.ks_stride_page, a.ks_stride_row, a.ks_stride_head, a.vs_stride_page, a.vs_stride_row, a.vs_stride_head};
+    if (const char* why = nvfp4_scales_problem(a.k_scales, a.v_scales, st, false))
+      return fail(MJ_ERR_INVALID, "mj_cache_write: %s", why);
+  }
   return cuda_status(mj::launch_cache_write(a, (cudaStream_t)stream), "mj_cache_write launch");
 }
 
@@ -89,8 +109,13 @@ static int validate_decode(const mj_decode_args& a, const char* who) {
     return fail(MJ_ERR_INVALID, "%s: num_seqs %d q_len %d h_q %d h_k %d", who, a.num_seqs, a.q_len, a.h_q, a.h_k);
   if (a.head_size != 128 && a.head_size != 256)
     return fail(MJ_ERR_UNSUPPORTED, "%s: head_size %d (128 or 256)", who, a.head_size);
-  if (a.kv_format < MJ_KV_FP8_E4M3 || a.kv_format > MJ_KV_E2M1)
+  if (a.kv_format < MJ_KV_FP8_E4M3 || a.kv_format > MJ_KV_NVFP4)
     return fail(MJ_ERR_INVALID, "%s: kv_format %d", who, a.kv_format);
+  if (a.kv_format == MJ_KV_NVFP4) {
+    const int64_t st[6] = {a.ks_stride_page, a.ks_stride_row, a.ks_stride_head, a.vs_stride_page, a.vs_stride_row, a.vs_stride_head};
+    if (const char* why = nvfp4_scales_problem(a.k_scales, a.v_scales, st, false))
+      return fail(MJ_ERR_INVALID, "%s: %s", who, why);
+  }
   const int n_q = a.q_len * (a.h_q / a.h_k);
   if (n_q > 64) return fail(MJ_ERR_UNSUPPORTED, "%s: q_len * h_q / h_k = %d > 64 rows per KV head", who, n_q);
   if (a.q_dtype < MJ_DT_BF16 || a.q_dtype > MJ_DT_FP32 || a.o_dtype < MJ_DT_BF16 || a.o_dtype > MJ_DT_FP32)
@@ -175,6 +200,13 @@ int mj_expand_pages(const mj_expand_args* args, void* stream) {
                 (long long)a.num_out_pages, a.h_k, a.page_size, (long long)a.num_pages);
   if (a.head_size <= 0 || a.head_size % 16)
     return fail(MJ_ERR_UNSUPPORTED, "mj_expand_pages: head_size %d (a multiple of 16)", a.head_size);
+  if (a.kv_format < MJ_KV_E2M3 || a.kv_format > MJ_KV_NVFP4)
+    return fail(MJ_ERR_INVALID, "mj_expand_pages: kv_format %d (a narrow format)", a.kv_format);
+  if (a.kv_format == MJ_KV_NVFP4) {
+    const int64_t st[6] = {a.ks_stride_page, a.ks_stride_row, a.ks_stride_head, a.vs_stride_page, a.vs_stride_row, a.vs_stride_head};
+    if (const char* why = nvfp4_scales_problem(a.k_scales, a.v_scales, st, false))
+      return fail(MJ_ERR_INVALID, "mj_expand_pages: %s", why);
+  }
   if (a.num_out_pages == 0) {
     g_err[0] = 0;
     return MJ_OK;

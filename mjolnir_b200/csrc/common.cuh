@@ -26,6 +26,9 @@ __device__ __forceinline__ void store_elem(void* p, int64_t i, int dt, float v) 
   else reinterpret_cast<float*>(p)[i] = v;
 }
 
+// max that propagates NaN (as torch's amax does)
+__device__ __forceinline__ float nan_max(float a, float b) { return (a > b || a != a) ? a : b; }
+
 __device__ __forceinline__ void flag(int32_t* status, int code) {
   if (status) atomicExch(status, code);
 }
@@ -153,6 +156,14 @@ __device__ __forceinline__ uint8_t e4m3_byte(float x) {
 __device__ __forceinline__ float e4m3_value(uint8_t b) {
   __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
   return __half2float(__half(h));
+}
+
+// nvfp4: the e4m3 byte the tensor cores multiply for e2m1 code `code` of a
+// group with scale byte `sb`: e4m3(value(code) * value(sb) * 2^-3). The fp32
+// product is exact, so the one rounding is the e4m3 conversion
+// (quant.py:81-83).
+__device__ __forceinline__ uint8_t nvfp4_byte(uint32_t code, uint8_t sb) {
+  return e4m3_byte(e2m1_value(code) * e4m3_value(sb) * 0.125f);
 }
 
 // Descale of (seq, head) under a mode.

@@ -23,9 +23,10 @@ namespace mj {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-// 16 consecutive KV codes of a row starting at element c0 -> floats.
+// 16 consecutive KV codes of a row starting at element c0 -> floats (nvfp4:
+// the e4m3 values the tensor cores multiply, from the row's scale bytes).
 template <int FMT>
-__device__ __forceinline__ void load_codes16(const uint8_t* row, int c0, float* out) {
+__device__ __forceinline__ void load_codes16(const uint8_t* row, int c0, float* out, const uint8_t* srow = nullptr) {
   if (FMT == MJ_KV_FP8_E4M3) {
     uint4 raw = *reinterpret_cast<const uint4*>(row + c0);
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -40,13 +41,22 @@ __device__ __forceinline__ void load_codes16(const uint8_t* row, int c0, float* 
       out[4 * i + 2] = b.x;
       out[4 * i + 3] = b.y;
     }
-  } else if (FMT == MJ_KV_E2M1) {
+  } else if (FMT == MJ_KV_E2M1 || FMT == MJ_KV_NVFP4) {
     // 16 codes = 8 bytes at byte offset c0 / 2 (8-byte aligned), low nibble first
     const uint2 w = *reinterpret_cast<const uint2*>(row + (c0 >> 1));
+    if (FMT == MJ_KV_NVFP4) {
+      const uint8_t sb = srow[c0 >> 4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      out[k] = e2m1_value((w.x >> (4 * k)) & 15u);
-      out[8 + k] = e2m1_value((w.y >> (4 * k)) & 15u);
+      for (int k = 0; k < 8; ++k) {
+        out[k] = e4m3_value(nvfp4_byte((w.x >> (4 * k)) & 15u, sb));
+        out[8 + k] = e4m3_value(nvfp4_byte((w.y >> (4 * k)) & 15u, sb));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        out[k] = e2m1_value((w.x >> (4 * k)) & 15u);
+        out[8 + k] = e2m1_value((w.y >> (4 * k)) & 15u);
+      }
     }
   } else {
     // 16 codes = 12 bytes at byte offset c0 * 3 / 4 (4-byte aligned)
@@ -143,10 +153,13 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(const mj_decode_args a
     for (int r = 0; r < NQ; ++r) s[r] = 0.f;
     if (valid) {
       const uint8_t* krow = kbase + pg * a.k_stride_page + (int64_t)prow * a.k_stride_row;
+      const uint8_t* ksrow = FMT == MJ_KV_NVFP4 ? reinterpret_cast<const uint8_t*>(a.k_scales) + pg * a.ks_stride_page +
+                                                     (int64_t)prow * a.ks_stride_row + (int64_t)h * a.ks_stride_head
+                                               : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < D; c0 += 16) {
         float kv[16];
-        load_codes16<FMT>(krow, c0, kv);
+        load_codes16<FMT>(krow, c0, kv, ksrow);
 #pragma unroll
         for (int r = 0; r < NQ; ++r) {
           if (r < n_q) {
@@ -158,10 +171,13 @@ __global__ void __launch_bounds__(128) decode_simt_kernel(const mj_decode_args a
         }
       }
       const uint8_t* vrow = vbase + pg * a.v_stride_page + (int64_t)prow * a.v_stride_row;
+      const uint8_t* vsrow = FMT == MJ_KV_NVFP4 ? reinterpret_cast<const uint8_t*>(a.v_scales) + pg * a.vs_stride_page +
+                                                     (int64_t)prow * a.vs_stride_row + (int64_t)h * a.vs_stride_head
+                                               : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < D; c0 += 16) {
         float vv[16];
-        load_codes16<FMT>(vrow, c0, vv);
+        load_codes16<FMT>(vrow, c0, vv, vsrow);
 #pragma unroll
         for (int i = 0; i < 16; ++i) sm.v[tid][c0 + i] = __float2half_rn(vv[i]);
       }
@@ -372,6 +388,7 @@ static cudaError_t launch_simt_d(const mj_decode_args& a, int n_q, cudaStream_t 
     case MJ_KV_E2M3: return launch_simt_nq<D, MJ_KV_E2M3>(a, n_q, stream);
     case MJ_KV_E3M2: return launch_simt_nq<D, MJ_KV_E3M2>(a, n_q, stream);
     case MJ_KV_E2M1: return launch_simt_nq<D, MJ_KV_E2M1>(a, n_q, stream);
+    case MJ_KV_NVFP4: return launch_simt_nq<D, MJ_KV_NVFP4>(a, n_q, stream);
     default: return launch_simt_nq<D, MJ_KV_FP8_E4M3>(a, n_q, stream);
   }
 }

@@ -970,6 +970,7 @@ static EncodeTiledFn encode_fn() {
 
 // Why the tensor-core kernel cannot run these arguments (nullptr = it can).
 const char* tc_ineligible(const mj_decode_args& a) {
+  if (a.kv_format == MJ_KV_NVFP4) return "nvfp4 runs on the CUDA-core kernel";
   if (a.head_size != 128) return "head_size != 128";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";

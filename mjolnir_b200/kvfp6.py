@@ -22,7 +22,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .runner import _stream, dtype_code, kv_byte_strides, row_bytes as _row_bytes, scale_mode
+from .runner import _stream, dtype_code, kv_byte_strides, row_bytes as _row_bytes, scale_mode, set_scale_views
 
 E2M3_MAX = 7.5
 BITS = 6
@@ -43,6 +43,8 @@ def cache_write_args(
     v_scale: torch.Tensor,
     kv_format: str,
     status: torch.Tensor | None = None,
+    k_scales: torch.Tensor | None = None,
+    v_scales: torch.Tensor | None = None,
 ) -> _lib.CacheWriteArgs:
     """Validated ``mj_cache_write`` arguments for these tensors (they must
     stay alive while the returned struct is used)."""
@@ -78,6 +80,7 @@ def cache_write_args(
     a.k_scale, a.k_scale_mode = k_scale.data_ptr(), scale_mode(k_scale, h_k, d)
     a.v_scale, a.v_scale_mode = v_scale.data_ptr(), scale_mode(v_scale, h_k, d)
     a.status = None if status is None else status.data_ptr()
+    set_scale_views(a, k_scales, v_scales, k_cache.shape[0], k_cache.shape[1], h_k, d, kv_format)
     return a
 
 
@@ -91,15 +94,20 @@ def reshape_and_cache(
     v_scale: torch.Tensor,
     kv_format: str,
     status: torch.Tensor | None = None,
+    k_scales: torch.Tensor | None = None,  # nvfp4: (pages, page_size, h_k, d / 16) uint8 group-scale views
+    v_scales: torch.Tensor | None = None,
 ) -> None:
-    """Quantize, pack and scatter T new K/V rows into the cache views."""
+    """Quantize, pack and scatter T new K/V rows into the cache views (nvfp4:
+    k_scale / v_scale are the global scales, per tensor or per KV head, and the
+    group scale bytes go to k_scales / v_scales)."""
     if slot_mapping.shape[0] == 0:
         return
     if slot_mapping.dtype != torch.int64:
         slot_mapping = slot_mapping.to(torch.int64)
     k_scale = k_scale.to(torch.float32).contiguous()
     v_scale = v_scale.to(torch.float32).contiguous()
-    a = cache_write_args(key, value, k_cache, v_cache, slot_mapping, k_scale, v_scale, kv_format, status)
+    a = cache_write_args(key, value, k_cache, v_cache, slot_mapping, k_scale, v_scale, kv_format, status,
+                         k_scales, v_scales)
     _lib.cache_write(a, _stream(key.device))
 
 
@@ -127,7 +135,7 @@ def write_kv(
 
 
 def expand_pages(
-    k_cache: torch.Tensor,  # e2m3 logical (pages, page_size, h_k, row_bytes) uint8 view
+    k_cache: torch.Tensor,  # narrow logical (pages, page_size, h_k, row_bytes) uint8 view
     v_cache: torch.Tensor,
     src_pages: torch.Tensor,  # (P,) int32: cache page of each output page
     k_out: torch.Tensor,  # e4m3 logical (>= P, page_size, h_k, d) uint8 / float8 view
@@ -135,20 +143,27 @@ def expand_pages(
     k_ratio: torch.Tensor | None = None,  # fp32: 1 elem, (h_k,) or (h_k, d)
     v_ratio: torch.Tensor | None = None,
     status: torch.Tensor | None = None,
+    kv_format: str = "e2m3",
+    k_scales: torch.Tensor | None = None,  # nvfp4: (pages, page_size, h_k, d / 16) uint8 group-scale views
+    v_scales: torch.Tensor | None = None,
 ) -> None:
     """Expand P cache pages (K and V) to e4m3 bytes in output pages 0..P-1.
 
-    Without ratios the bytes are the e2m3 values exactly (the cache's scales
-    remain the descales). With per-channel scales s_c and a per-head descale S
-    of the reader, ratio = s_c / S makes each byte e4m3(code * s_c / S); a
-    reader without descales takes ratio = s_c (reference ``kvfp6.py:257-335``)."""
+    Without ratios the bytes are the code values exactly (e2m3, e2m1; e3m2
+    rounds to e4m3; nvfp4 gives the e4m3 values its tensor-core MMA reads and
+    keeps the gs * 2^3 descale). With per-channel scales s_c and a per-head
+    descale S of the reader, ratio = s_c / S makes each byte
+    e4m3(code * s_c / S); a reader without descales takes ratio = s_c
+    (reference ``kvfp6.py:257-335``)."""
     P = int(src_pages.shape[0])
     if P == 0:
         return
+    if kv_format not in ("e2m3", "e3m2", "e2m1", "nvfp4"):
+        raise ValueError(f"page expansion reads a narrow format, not {kv_format!r}")
     _, N, h_k, rb = k_cache.shape
-    d = rb * 4 // 3
-    if rb != row_bytes(d) or v_cache.shape != k_cache.shape:
-        raise ValueError(f"e2m3 views {tuple(k_cache.shape)} / {tuple(v_cache.shape)}")
+    d = rb * 2 if kv_format in ("e2m1", "nvfp4") else rb * 4 // 3
+    if rb != _row_bytes(d, kv_format) or v_cache.shape != k_cache.shape:
+        raise ValueError(f"{kv_format} views {tuple(k_cache.shape)} / {tuple(v_cache.shape)}")
     for t in (k_out, v_out):
         if t.dim() != 4 or t.shape[0] < P or tuple(t.shape[1:]) != (N, h_k, d) or t.element_size() != 1:
             raise ValueError(f"output view {tuple(t.shape)} is not (>= {P}, {N}, {h_k}, {d}) bytes")
@@ -175,4 +190,6 @@ def expand_pages(
         setattr(a, f"{side}_ratio", ptr)
         setattr(a, f"{side}_ratio_mode", mode)
     a.status = None if status is None else status.data_ptr()
+    a.kv_format = _lib.KV_FORMATS[kv_format]
+    set_scale_views(a, k_scales, v_scales, k_cache.shape[0], N, h_k, d, kv_format)
     _lib.expand_pages(a, _stream(k_cache.device))

@@ -131,9 +131,34 @@ def row_bytes(head_size: int, kv_format: str) -> int:
         return head_size
     if kv_format in ("e2m3", "e3m2"):
         return head_size * 3 // 4
-    if kv_format == "e2m1":
+    if kv_format in ("e2m1", "nvfp4"):
         return head_size // 2
     raise ValueError(f"kv_format {kv_format!r}")
+
+
+NVFP4_GROUP = 16
+
+
+def scale_row_bytes(head_size: int) -> int:
+    """Bytes of one nvfp4 scale row: one e4m3 byte per 16 elements."""
+    return head_size // NVFP4_GROUP
+
+
+def set_scale_views(a, k_scales: torch.Tensor | None, v_scales: torch.Tensor | None, pages: int, page_size: int,
+                    h_k: int, head_size: int, kv_format: str) -> None:
+    """Point an args struct at the nvfp4 group-scale views (logical
+    (pages, page_size, h_k, head_size / 16) bytes, last dim contiguous)."""
+    if kv_format != "nvfp4":
+        return
+    want = (page_size, h_k, scale_row_bytes(head_size))
+    for name, t in (("k_scales", k_scales), ("v_scales", v_scales)):
+        if t is None:
+            raise ValueError("nvfp4 needs k_scales and v_scales")
+        if t.dim() != 4 or tuple(t.shape[1:]) != want or t.shape[0] < pages or t.element_size() != 1:
+            raise ValueError(f"{name} view {tuple(t.shape)} is not (>= {pages}, {want[0]}, {want[1]}, {want[2]}) bytes")
+    a.k_scales, a.v_scales = k_scales.data_ptr(), v_scales.data_ptr()
+    a.ks_stride_page, a.ks_stride_row, a.ks_stride_head = kv_byte_strides(k_scales)
+    a.vs_stride_page, a.vs_stride_row, a.vs_stride_head = kv_byte_strides(v_scales)
 
 
 _DT = {torch.bfloat16: _lib.MJ_DT_BF16, torch.float16: _lib.MJ_DT_FP16, torch.float32: _lib.MJ_DT_FP32}
@@ -357,6 +382,8 @@ class DecodeRunner:
         q_mul: torch.Tensor | None = None,
         o_mul: torch.Tensor | None = None,
         lse: torch.Tensor | None = None,
+        k_scales: torch.Tensor | None = None,
+        v_scales: torch.Tensor | None = None,
     ) -> _lib.DecodeArgs:
         b, ql = plan.num_seqs, plan.q_len
         tokens = b * ql
@@ -403,6 +430,7 @@ class DecodeRunner:
         a.kernel = self.kernel
         a.status = self.status.data_ptr()
         a.merge_counters = self.merge_counters.data_ptr() if self.fused_merge else None
+        set_scale_views(a, k_scales, v_scales, k_cache.shape[0], self.page_size, self.h_k, self.d, self.kv_format)
         return a
 
     def merges_in_kernel(self, args: _lib.DecodeArgs) -> bool:
@@ -425,8 +453,11 @@ class DecodeRunner:
         q_mul: torch.Tensor | None = None,  # (h_q, d) fp32: e2m3 K channel scales folded into Q
         o_mul: torch.Tensor | None = None,  # (h_q, d) fp32: e2m3 V channel scales on O
         lse: torch.Tensor | None = None,  # optional (b*q_len, h_q) fp32
+        k_scales: torch.Tensor | None = None,  # nvfp4: (num_pages, page_size, h_k, d / 16) uint8 views
+        v_scales: torch.Tensor | None = None,
     ):
-        a = self.decode_args(plan, query, out, k_cache, v_cache, k_scale, v_scale, softmax_scale, q_mul, o_mul, lse)
+        a = self.decode_args(plan, query, out, k_cache, v_cache, k_scale, v_scale, softmax_scale, q_mul, o_mul, lse,
+                             k_scales, v_scales)
         _lib.decode(a, _stream(self.device))
         return out
 

@@ -30,9 +30,13 @@ import torch
 from . import quant
 
 
-def dequant_pool(pool_bytes: np.ndarray | torch.Tensor, kv_format: str, d: int) -> torch.Tensor:
-    """(pages, PS, h_k, row_bytes) uint8 -> (pages, PS, h_k, d) float32 code values."""
+def dequant_pool(pool_bytes: np.ndarray | torch.Tensor, kv_format: str, d: int, scales=None) -> torch.Tensor:
+    """(pages, PS, h_k, row_bytes) uint8 -> (pages, PS, h_k, d) float32 code values
+    (nvfp4: the e4m3 kernel values from the (pages, PS, h_k, d / 16) scale bytes)."""
     b = pool_bytes.numpy() if isinstance(pool_bytes, torch.Tensor) else np.asarray(pool_bytes)
+    if kv_format == "nvfp4":
+        sc = scales.numpy() if isinstance(scales, torch.Tensor) else np.asarray(scales)
+        return torch.from_numpy(quant.decode_rows_nvfp4(b, sc, d))
     if kv_format == "fp8":
         return torch.from_numpy(quant.decode_fp8(b))
     if kv_format == "e2m3":
@@ -130,6 +134,7 @@ def merge_splits(o_parts: torch.Tensor, lse_parts: torch.Tensor):
 
 
 def kv_bytes(seq_lens, h_k: int, d: int, kv_format: str) -> int:
-    """Algorithmic KV bytes one decode step streams: sum(L) * h_k * 2 rows."""
-    row = d if kv_format == "fp8" else d * 3 // 4
+    """Algorithmic KV bytes one decode step streams: sum(L) * h_k * 2 rows
+    (nvfp4 rows carry their d / 16 scale bytes)."""
+    row = {"fp8": d, "e2m3": d * 3 // 4, "e3m2": d * 3 // 4, "e2m1": d // 2, "nvfp4": d // 2 + d // 16}[kv_format]
     return int(sum(int(x) for x in seq_lens)) * h_k * 2 * row

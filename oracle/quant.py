@@ -184,13 +184,20 @@ def scale_mode(n: int, h_k: int, d: int) -> int:
     return 1 if n == h_k and h_k > 1 else 0
 
 
-def expand_rows_e4m3(packed: np.ndarray, d: int, ratio=None) -> np.ndarray:
-    """packed e2m3 rows (..., h_k, 3d/4) -> e4m3 bytes (..., h_k, d):
+def expand_rows_e4m3(packed: np.ndarray, d: int, ratio=None, fmt: str = "e2m3", sc=None) -> np.ndarray:
+    """packed narrow rows (..., h_k, row) -> e4m3 bytes (..., h_k, d):
     ``e4m3(code_value * ratio)`` with the product in float32, round to nearest
-    even, saturating at +-448; ratio None gives the code values exactly.
-    Restates the page expansion of reference ``kvfp6.py:157-205`` (the RATIO
-    branch of ``_expand_kernel``: value LUT x ratio, then the fp8 cast)."""
-    vals = decode_rows_e2m3(packed, d).astype(np.float32)
+    even, saturating at +-448; ratio None gives the code values exactly (e2m3,
+    e2m1; e3m2 codes round). nvfp4's code value is its kernel value
+    e4m3(code * scale * 2^-3) from the scale bytes ``sc``. Restates the page
+    expansion of reference ``kvfp6.py:157-205`` (the RATIO branch of
+    ``_expand_kernel``: value LUT x ratio, then the fp8 cast)."""
+    if fmt == "nvfp4":
+        vals = decode_rows_nvfp4(packed, sc, d).astype(np.float32)
+    elif fmt == "e2m3":
+        vals = decode_rows_e2m3(packed, d).astype(np.float32)
+    else:
+        vals = decode_rows_narrow(packed, d, fmt).astype(np.float32)
     if ratio is not None:
         h_k = packed.shape[-2]
         vals = (vals * _expand_scale(ratio, h_k, d)).astype(np.float32)
@@ -269,3 +276,89 @@ def decode_rows_narrow(packed: np.ndarray, d: int, fmt: str) -> np.ndarray:
     """Packed rows of `fmt` -> code values (..., d) float32 (no scale)."""
     codes = unpack6(packed, d) if BITS[fmt] == 6 else unpack4(packed, d)
     return minifloat_table(fmt)[codes.astype(np.int64)]
+
+
+# ---------------------------------------------------------------------------
+# nvfp4 (reference quant.py:9-10, :68-84; the kernel-side conversion of
+# arch/thor/decode.py:980-1030 and the harness pool of
+# arch/thor/harness.py:579-586): e2m1 codes packed two per byte (low nibble
+# first), one e4m3 scale per group of 16 elements along d, one fp32 global
+# scale gs. The quantizer, in fp32 with gs rounded to fp32 as torch does for a
+# Python scalar operand:
+#   sc   = e4m3(min(amax_group / 6 / gs, 448))       (round to nearest even)
+#   q    = x / (value(sc) * gs)   (0 where that product is 0)
+#   code = e2m1(q)                (the narrow formats' rounding rule)
+# The tensor cores multiply e4m3(value(code) * value(sc) * 2^-3) -- exact
+# product, one rounding to e4m3 -- with the descale gs * 2^3.
+# ---------------------------------------------------------------------------
+NVFP4_GROUP = 16
+NVFP4_SHIFT = 0.125
+
+
+def nvfp4_global_scale(x: np.ndarray) -> float:
+    """gs = max(amax|x|, 1e-12) / (6 * 448), the reference's per-tensor choice
+    (the amax in fp32, the division in double)."""
+    amax = np.float32(np.max(np.abs(np.asarray(x, dtype=np.float32))))
+    return float(max(amax, np.float32(1e-12))) / (6.0 * 448.0)
+
+
+def nvfp4_quantize(x: np.ndarray, gs: float | None = None, group: int = NVFP4_GROUP):
+    """(..., d) float32 -> (codes (..., d) uint8, scale bytes (..., d/group) uint8,
+    gs, kernel e4m3 bytes (..., d) uint8, descale gs / 2^-3) -- the outputs of
+    the reference's ``nvfp4_quantize`` with the kernel values as e4m3 bytes.
+    gs None computes the reference's per-tensor global scale."""
+    x = np.asarray(x, dtype=np.float32)
+    if gs is None:
+        gs = nvfp4_global_scale(x)
+    g32 = np.float32(gs)
+    *lead, d = x.shape
+    xg = x.reshape(*lead, d // group, group)
+    amax_g = np.max(np.abs(xg), axis=-1)
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        sc_f = ((amax_g / np.float32(6.0)).astype(np.float32) / g32).astype(np.float32)
+        sc_f = np.where(sc_f > np.float32(FP8_MAX), np.float32(FP8_MAX), sc_f)  # NaN stays NaN
+        sc = e4m3_bytes(sc_f)
+        scf = decode_fp8(sc)
+        denom = (scf * g32).astype(np.float32)[..., None]
+        q = np.where(denom > 0, xg / np.maximum(denom, np.float32(1e-30)), np.float32(0)).astype(np.float32)
+    codes = minifloat_codes(q, "e2m1").reshape(*lead, d)
+    kern = nvfp4_kernel_bytes(codes, sc, group)
+    return codes, sc, gs, kern, gs / NVFP4_SHIFT
+
+
+def nvfp4_kernel_bytes(codes: np.ndarray, sc: np.ndarray, group: int = NVFP4_GROUP) -> np.ndarray:
+    """e2m1 codes (..., d) and scale bytes (..., d/group) -> the e4m3 bytes the
+    tensor cores read: e4m3(value(code) * value(sc) * 2^-3)."""
+    codes = np.asarray(codes).astype(np.int64)
+    *lead, d = codes.shape
+    lut = minifloat_table("e2m1")
+    scf = decode_fp8(np.asarray(sc, dtype=np.uint8)).astype(np.float32)
+    v = (lut[codes].reshape(*lead, d // group, group) * scf[..., None]).astype(np.float32)
+    v = (v * np.float32(NVFP4_SHIFT)).astype(np.float32)
+    return e4m3_bytes(v.reshape(*lead, d))
+
+
+def quantize_rows_nvfp4(x: np.ndarray, gs) -> tuple[np.ndarray, np.ndarray]:
+    """(..., h_k, d) float32 -> (packed codes (..., h_k, d/2), scale bytes
+    (..., h_k, d/16)) under a global scale per tensor (1 element) or per KV head
+    ((h_k,)) -- the quantize-on-write of an nvfp4 cache."""
+    x = np.asarray(x, dtype=np.float32)
+    g = np.asarray(gs, dtype=np.float64).reshape(-1)
+    if g.size == 1:
+        codes, sc, *_ = nvfp4_quantize(x, float(g[0]))
+        return pack4(codes), sc
+    h_k = x.shape[-2]
+    assert g.size == h_k, "nvfp4 global scale: 1 element or one per KV head"
+    packed = np.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=np.uint8)
+    sc = np.empty(x.shape[:-1] + (x.shape[-1] // NVFP4_GROUP,), dtype=np.uint8)
+    for h in range(h_k):
+        c, s, *_ = nvfp4_quantize(x[..., h, :], float(g[h]))
+        packed[..., h, :] = pack4(c)
+        sc[..., h, :] = s
+    return packed, sc
+
+
+def decode_rows_nvfp4(packed: np.ndarray, sc: np.ndarray, d: int) -> np.ndarray:
+    """Packed nvfp4 rows and their scale bytes -> the kernel values (float32,
+    before the gs * 2^3 descale)."""
+    return decode_fp8(nvfp4_kernel_bytes(unpack4(packed, d), sc))

@@ -9,6 +9,7 @@ the development container:
 
 Reference functions exercised:
   quant.minifloat_quantize / pack_subbyte     (src/mjolnir/mjolnir/quant.py:34-65)
+  quant.nvfp4_quantize                        (src/mjolnir/mjolnir/quant.py:68-84)
   kvfp6.quantize_rows_reference / decode_...  (src/mjolnir/mjolnir/kvfp6.py:342-365)
   the fp8 cache write (x / s).to(e4m3)        (src/mjolnir/mjolnir/arch/thor/harness.py:588-590)
   arch.orin.harness.ref_decode                (src/mjolnir/mjolnir/arch/orin/harness.py:31-79)
@@ -91,6 +92,36 @@ def gen_narrow(quant):
             codes, _ = quant.minifloat_quantize(x / s, fmt)
             out[f"{fmt}_all_{name}"] = quant.pack_subbyte(codes, bits).numpy()
         out[f"{fmt}_table"] = quant.minifloat_table(fmt).numpy()
+    return out
+
+
+def gen_nvfp4(quant):
+    """nvfp4 (quant.py:68-84): codes, e4m3 group scales, global scale, kernel
+    values and descale of the reference's nvfp4_quantize on seeded inputs --
+    random rows at three magnitudes with zeroed elements, zero groups and
+    outliers, and every bf16 value of magnitude 2^-27 .. 2^13 (both signs)."""
+    out = {}
+    g = torch.Generator().manual_seed(4)
+    cases = {}
+    for i, mag in enumerate((1e-3, 1.0, 50.0)):
+        x = torch.randn(3, 8, 128, generator=g) * mag
+        x[torch.rand(x.shape, generator=g) < 0.2] = 0.0
+        x[0, 0, :16] = 0.0  # a zero group
+        x[1, 2, 5] *= 40.0  # an outlier
+        cases[f"rand{i}"] = x
+    bits = torch.arange(65536, dtype=torch.int32)
+    expo = (bits >> 7) & 0xFF
+    keep = bits[(expo >= 100) & (expo <= 140)]
+    keep = keep[torch.randperm(keep.numel(), generator=g)]
+    n = keep.numel() // 1024 * 1024
+    cases["bf16"] = (keep[:n].to(torch.int16).view(torch.bfloat16).float()).reshape(-1, 8, 128)
+    for name, x in cases.items():
+        codes, sc, gs, vals, desc = quant.nvfp4_quantize(x.clone())
+        out[f"{name}__x"] = x.numpy()
+        out[f"{name}__codes"] = quant.pack_subbyte(codes, 4).numpy()
+        out[f"{name}__sc"] = sc.view(torch.uint8).numpy()
+        out[f"{name}__gs"] = np.array([gs, desc], dtype=np.float64)
+        out[f"{name}__kern"] = vals.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
     return out
 
 
@@ -217,9 +248,10 @@ def main():
     torch.manual_seed(0)
     np.savez_compressed(os.path.join(HERE, "quant.npz"), **gen_quant(kvfp6))
     np.savez_compressed(os.path.join(HERE, "narrow.npz"), **gen_narrow(quant))
+    np.savez_compressed(os.path.join(HERE, "nvfp4.npz"), **gen_nvfp4(quant))
     np.savez_compressed(os.path.join(HERE, "decode.npz"), **gen_decode(kvfp6, ref_decode, emulate_decode))
     np.savez_compressed(os.path.join(HERE, "plan.npz"), **gen_plan(plan_split_kv))
-    for f in ("quant.npz", "narrow.npz", "decode.npz", "plan.npz"):
+    for f in ("quant.npz", "narrow.npz", "nvfp4.npz", "decode.npz", "plan.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

@@ -76,14 +76,27 @@ class Case:
                     raw["k"][bt[s, bi]] *= (1.0 + k_ramp * pos / L).view(page_size, 1, 1)
         if kv_format == "fp8":
             self.k_scale_w = self.v_scale_w = torch.ones(1)
+        elif kv_format == "nvfp4":
+            # the reference harness's choice: one global scale per tensor (quant.py:74)
+            self.k_scale_w = torch.tensor([quant.nvfp4_global_scale(raw["k"].to(torch.bfloat16).float().numpy())])
+            self.v_scale_w = torch.tensor([quant.nvfp4_global_scale(raw["v"].to(torch.bfloat16).float().numpy())])
         else:
             # per (KV head, channel) amax / the format's max (kvscales.e2m3_scales without headroom)
             self.k_scale_w = raw["k"].abs().amax(dim=(0, 1)).clamp(min=1e-6) / vmax
             self.v_scale_w = raw["v"].abs().amax(dim=(0, 1)).clamp(min=1e-6) / vmax
         self.bytes = {}
         self.vals = {}
+        self.group_scales = {}
         for side, sc in (("k", self.k_scale_w), ("v", self.v_scale_w)):
             xb = raw[side].to(torch.bfloat16).float().numpy()
+            if kv_format == "nvfp4":
+                by, gsc = quant.quantize_rows_nvfp4(xb, sc.double().numpy())
+                by[unused] = 0x77  # code +6 in both nibbles
+                gsc[unused] = 0x7E  # scale 448 (the reference harness's poison, harness.py:581-583)
+                self.group_scales[side] = torch.from_numpy(gsc)
+                self.bytes[side] = torch.from_numpy(by)
+                self.vals[side] = attention.dequant_pool(by, kv_format, d, gsc)
+                continue
             if kv_format == "fp8":
                 by = quant.quantize_rows_fp8(xb, sc.numpy())
                 by[unused] = FP8_NAN
@@ -101,12 +114,25 @@ class Case:
         self.k_view, self.v_view = split_kv_cache(cache, layout, rb)
         self.k_view.copy_(self.bytes["k"].to(device))
         self.v_view.copy_(self.bytes["v"].to(device))
+        self.k_scales = self.v_scales = None
+        if kv_format == "nvfp4":
+            # group scales in their own tensor, K and V interleaved per row:
+            # (pages, page_size, h_k, 2, d / 16), so both views are strided
+            sc_dev = torch.empty(self.num_pages, page_size, h_k, 2, d // 16, dtype=torch.uint8, device=device)
+            self.k_scales, self.v_scales = sc_dev[:, :, :, 0], sc_dev[:, :, :, 1]
+            self.k_scales.copy_(self.group_scales["k"].to(device))
+            self.v_scales.copy_(self.group_scales["v"].to(device))
+            self.scale_cache = sc_dev
         self.block_table = bt.to(device)
         sl = torch.zeros(self.max_num_seqs, dtype=torch.int32)
         sl[:b] = torch.tensor(self.seq_lens, dtype=torch.int32)
         self.seq_lens_t = sl.to(device)
-        # descales (fp8) -- e2m3 uses the channel scales through q_mul / o_mul
-        if kv_format == "fp8":
+        # descales (fp8; nvfp4: gs * 2^3) -- e2m3 uses the channel scales through q_mul / o_mul
+        if kv_format == "nvfp4":
+            self.kd = (self.k_scale_w.double() / quant.NVFP4_SHIFT).float()
+            self.vd = (self.v_scale_w.double() / quant.NVFP4_SHIFT).float()
+            self.q_mul = self.o_mul = None
+        elif kv_format == "fp8":
             if descale == "tensor":
                 self.kd, self.vd = torch.tensor([1.0]), torch.tensor([1.0])
             elif descale == "head":
@@ -154,7 +180,8 @@ class Case:
         out = torch.full((T + 2, self.h_q * self.d), float("nan"), dtype=out_dtype, device=self.query.device)
         lse_t = torch.full((T, self.h_q), float("nan"), device=self.query.device) if lse else None
         r.run(plan, self.query, out, self.k_view, self.v_view, self.dev(self.kd), self.dev(self.vd),
-              1.0 / math.sqrt(self.d), q_mul=self.dev(self.q_mul), o_mul=self.dev(self.o_mul), lse=lse_t)
+              1.0 / math.sqrt(self.d), q_mul=self.dev(self.q_mul), o_mul=self.dev(self.o_mul), lse=lse_t,
+              k_scales=self.k_scales, v_scales=self.v_scales)
         torch.cuda.synchronize()
         r.check_status()
         return out, lse_t, plan

@@ -144,3 +144,21 @@ def test_narrow_formats_bit_exact_on_every_bf16(fmt):
         np.testing.assert_array_equal(got, g[f"{fmt}_all_{name}"], err_msg=f"{fmt} scale {s}")
         d = quant.decode_rows_narrow(got, 128, fmt)
         assert np.all(np.abs(d) <= quant.minifloat_table(fmt).max())
+
+
+@pytest.mark.parametrize("case", ["rand0", "rand1", "rand2", "bf16"])
+def test_nvfp4_matches_reference(case):
+    """nvfp4: the oracle's codes, group scales, global scale, kernel e4m3
+    values and descale equal the reference's nvfp4_quantize (quant.py:68-84)."""
+    g = np.load(os.path.join(GOLDEN, "nvfp4.npz"))
+    x = g[f"{case}__x"]
+    codes, sc, gs, kern, desc = quant.nvfp4_quantize(x)
+    assert gs == g[f"{case}__gs"][0] and desc == g[f"{case}__gs"][1]
+    np.testing.assert_array_equal(quant.pack4(codes), g[f"{case}__codes"])
+    np.testing.assert_array_equal(sc, g[f"{case}__sc"])
+    np.testing.assert_array_equal(kern, g[f"{case}__kern"])
+    # the write form (per-tensor gs) gives the same bytes, and decodes to the kernel values
+    packed, sc2 = quant.quantize_rows_nvfp4(x, np.float64(gs))
+    np.testing.assert_array_equal(packed, g[f"{case}__codes"])
+    np.testing.assert_array_equal(sc2, sc)
+    np.testing.assert_array_equal(quant.decode_rows_nvfp4(packed, sc2, x.shape[-1]), quant.decode_fp8(kern))
