@@ -103,14 +103,58 @@ __device__ __forceinline__ uint4 e2m1x16_to_e4m3(uint4 raw) {
                     e2m1_bytes(__byte_perm(e1, o1, 0x5140)), e2m1_bytes(__byte_perm(e1, o1, 0x7362)));
 }
 
+// nvfp4: 16 e2m1 codes (the first 8 bytes of a 16U4 slot, low nibble first)
+// of one scale group -> 16 e4m3 bytes e4m3(value(code) * scale * 2^-3).
+// s2 holds scale * 2^-3 in both f16 halves. value(code) (<= 2 significant
+// bits) times an e4m3 scale (<= 4) is exact in f16, as is the 2^-3, so the one
+// rounding is the e4m3 conversion (nearest even) -- the reference's fp32
+// arithmetic (quant.py:81-83) gives the same bytes.
+__device__ __forceinline__ uint4 nvfp4x16_to_e4m3(uint4 raw, uint32_t s2) {
+  uint4 o;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3, b4, b5, b6, b7;\n\t"
+      ".reg .b32 h0, h1, h2, h3, h4, h5, h6, h7;\n\t"
+      ".reg .b16 e0, e1, e2, e3, e4, e5, e6, e7;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "mov.b32 {b4, b5, b6, b7}, %5;\n\t"
+      "cvt.rn.f16x2.e2m1x2 h0, b0;\n\tcvt.rn.f16x2.e2m1x2 h1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 h2, b2;\n\tcvt.rn.f16x2.e2m1x2 h3, b3;\n\t"
+      "cvt.rn.f16x2.e2m1x2 h4, b4;\n\tcvt.rn.f16x2.e2m1x2 h5, b5;\n\t"
+      "cvt.rn.f16x2.e2m1x2 h6, b6;\n\tcvt.rn.f16x2.e2m1x2 h7, b7;\n\t"
+      "mul.rn.f16x2 h0, h0, %6;\n\tmul.rn.f16x2 h1, h1, %6;\n\t"
+      "mul.rn.f16x2 h2, h2, %6;\n\tmul.rn.f16x2 h3, h3, %6;\n\t"
+      "mul.rn.f16x2 h4, h4, %6;\n\tmul.rn.f16x2 h5, h5, %6;\n\t"
+      "mul.rn.f16x2 h6, h6, %6;\n\tmul.rn.f16x2 h7, h7, %6;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f16x2 e0, h0;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e1, h1;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f16x2 e2, h2;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e3, h3;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f16x2 e4, h4;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e5, h5;\n\t"
+      "cvt.rn.satfinite.e4m3x2.f16x2 e6, h6;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e7, h7;\n\t"
+      "mov.b32 %0, {e0, e1};\n\tmov.b32 %1, {e2, e3};\n\t"
+      "mov.b32 %2, {e4, e5};\n\tmov.b32 %3, {e6, e7};\n\t}"
+      : "=r"(o.x), "=r"(o.y), "=r"(o.z), "=r"(o.w)
+      : "r"(raw.x), "r"(raw.y), "r"(s2));
+  return o;
+}
+
+// scale byte -> f16x2 (scale * 2^-3, both halves); a NaN byte (never written
+// by the quantizer, possible in unwritten rows) reads as 0
+__device__ __forceinline__ uint32_t nvfp4_scale2(uint32_t sb) {
+  sb = (sb & 0x7Fu) == 0x7Fu ? 0u : sb;
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((unsigned short)(sb | (sb << 8))));
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x30003000u));  // x 2^-3
+  return r;
+}
+
 // Per-format constants of the tensor-core path.
 template <int FMT>
 struct Fmt {
   static constexpr bool NARROW = FMT != MJ_KV_FP8_E4M3;  // V needs a conversion to e4m3
-  // kind::f8f6f4 operand format of K
+  static constexpr bool SCALED = FMT == MJ_KV_NVFP4;     // group scales: K is converted too
+  // kind::f8f6f4 operand format of K (nvfp4 K is converted to e4m3)
   static constexpr uint32_t MMA_FMT = FMT == MJ_KV_E2M3 ? 3u : FMT == MJ_KV_E3M2 ? 4u : FMT == MJ_KV_E2M1 ? 5u : 0u;
-  static constexpr uint32_t ROW = FMT == MJ_KV_E2M1 ? 64u : NARROW ? 96u : 128u;  // packed bytes per 128-code row
-  static constexpr float V_UNSCALE = FMT == MJ_KV_E3M2 ? 16.f : NARROW ? 64.f : 1.f;  // undoes the conversion's shift
+  static constexpr uint32_t ROW = (FMT == MJ_KV_E2M1 || SCALED) ? 64u : NARROW ? 96u : 128u;  // packed bytes per 128-code row
+  static constexpr float V_UNSCALE = FMT == MJ_KV_E3M2 ? 16.f : SCALED ? 1.f : NARROW ? 64.f : 1.f;  // undoes the conversion's shift
   static __device__ __forceinline__ uint4 convert(uint4 raw) {
     if constexpr (FMT == MJ_KV_E3M2) return e3m2x16_to_e4m3(raw);
     else if constexpr (FMT == MJ_KV_E2M1) return e2m1x16_to_e4m3(raw);
@@ -140,7 +184,9 @@ struct Cfg {
   static constexpr int NO = (3 * RT + 15) / 16 * 16;     // PV MMA N (P is MN-major: multiples of 16)
   static constexpr int QBYTES = NS * 128;                // one K-major Q operand
   static constexpr int PBYTES = NO * 128;                // one MN-major P operand: NO/16 groups of [128 s][16 B]
-  static constexpr int STAGES = NWG == 1 ? (NQP <= 8 ? 3 : 2) : NWG == 2 ? 5 : 4;
+  // (nvfp4 at 8 rows: its scale copies leave room for two stages at two CTAs per SM)
+  static constexpr int STAGES = NWG == 1 ? (NQP <= 4 || (NQP == 8 && !Fmt<FMT>::SCALED) ? 3 : 2) : NWG == 2 ? 5 : 4;
+  static_assert(!Fmt<FMT>::SCALED || CVTW == 1, "nvfp4 converts K on the converter warpgroup only");
   static constexpr int TCOLS = 2 * NS + NO;              // S0 S1 O (O accumulates over a job's tiles)
   static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
   static_assert(TCOLS * CTAS_PER_SM <= 512, "the CTAs of an SM share its 512 TMEM columns");
@@ -160,14 +206,18 @@ struct Cfg {
   static constexpr int Q_OFF = V_OFF + STAGES * kTileBytes;  // two slots (jobs)
   static constexpr int P_OFF = (Q_OFF + 2 * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
   static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;
-  static constexpr int NBARS = 4 * STAGES + 2 * 8 + 1;  // k/v full/empty rings, 8 pairs, drain
+  static constexpr int NBARS = 5 * STAGES + 2 * 8 + 1;  // k/v full/empty rings, k_ready ring, 8 pairs, drain
   static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[NWG][2][4][NQP]
   static constexpr int MISC_OFF = RED_OFF + NWG * 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [NWG][4][NQP]
-  static constexpr int SMEM = MISC_OFF + 64 + NWG * 4 * 4 * NQP;
+  // nvfp4: per stage the K then V scale rows of the tile ([128 rows][8 B] each)
+  static constexpr int SC_OFF = (MISC_OFF + 64 + NWG * 4 * 4 * NQP + 15) / 16 * 16;
+  static constexpr int SC_BYTES = Fmt<FMT>::SCALED ? STAGES * 2 * 128 * 8 : 0;
+  static constexpr int SMEM = SC_OFF + SC_BYTES;
 };
 
 struct Bars {
   uint64_t *k_full, *k_empty, *v_full, *v_empty;               // TMA rings
+  uint64_t* k_ready;                                          // nvfp4: K tile converted (ring)
   uint64_t *s_full, *s_free, *p_full, *o_full, *v_ready, *v_free, *q_full;  // pairs (o_full: PV of tile t done)
   uint64_t* o_free;                                         // once per job: O read out, next job may overwrite
   uint64_t* drain;
@@ -276,6 +326,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   b.v_free = b.v_ready + 2;
   b.q_full = b.v_free + 2;
   b.drain = b.q_full + 2;
+  b.k_ready = b.drain + 1;
   float* red_all = reinterpret_cast<float*>(sm + C::RED_OFF);   // [NWG][2][4][NQP]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::MISC_OFF + 4);
@@ -283,11 +334,14 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   float* lred_all = reinterpret_cast<float*>(sm + C::MISC_OFF + 64);  // [NWG][4][NQP]
 
   if (threadIdx.x == 0) {
+    // nvfp4: the 32 TMA-warp lanes' scale copies also arrive on the full barriers
+    constexpr int FULL = 1 + (Fmt<FMT>::SCALED ? 32 : 0);
     for (int i = 0; i < S; ++i) {
-      mbar_init(&b.k_full[i], 1);
+      mbar_init(&b.k_full[i], FULL);
       mbar_init(&b.k_empty[i], 1);
-      mbar_init(&b.v_full[i], 1);
+      mbar_init(&b.v_full[i], FULL);
       mbar_init(&b.v_empty[i], 1);  // released by the PV MMA
+      mbar_init(&b.k_ready[i], C::CVT_ROLE);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b.s_full[i], 1);
@@ -330,6 +384,8 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   // byte offset of 16-byte chunk c (row c / 8) of the V tile, and of row r
   auto vchunk = [&](int c) { return (uint32_t)((c >> 6) * ATOM + (c & 63) * 16); };
   auto qbuf = [&](int i) { return sm + C::Q_OFF + i * C::QBYTES; };
+  auto kscl = [&](int st) { return sm + C::SC_OFF + st * 2048; };  // nvfp4 K scale rows of a stage
+  auto vscl = [&](int st) { return sm + C::SC_OFF + st * 2048 + 1024; };
   auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::PBYTES; };
   auto give_up = [&]() {
     *abort_flag = 1;
@@ -348,6 +404,20 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
     return te > tb;
   };
 
+  // nvfp4: convert a K or V tile in place (thread ct of the converter role
+  // takes chunks ct, ct + CVT_ROLE, ...): the 16 codes of a 16U4 slot are one
+  // scale group, whose logical index within the row is the slot's swizzled
+  // position XOR the row (mod 8); rows at or past `valid` become zeros.
+  auto nvfp4_tile = [&](unsigned char* buf, const unsigned char* scl, int valid, int ct) {
+#pragma unroll 2
+    for (int c = ct; c < kTileBytes / 16; c += C::CVT_ROLE) {
+      const int r = c >> 3;
+      uint4* q = reinterpret_cast<uint4*>(buf + vchunk(c));
+      if (r < valid) *q = nvfp4x16_to_e4m3(*q, nvfp4_scale2(scl[r * 8 + ((c ^ r) & 7)]));
+      else *q = make_uint4(0, 0, 0, 0);
+    }
+  };
+
   // ---------------------------------------- V conversion / tail zero (thread ct)
   auto convert_role = [&](const int ct) {
     int it = 0;
@@ -358,11 +428,20 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       const int L = a.seq_lens[seq];
       for (int tile = tb; tile < te; ++tile, ++it) {
         const int st = it % S;
+        if constexpr (Fmt<FMT>::SCALED) {  // K first: the S MMA waits for it (k_ready)
+          ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS);
+          if (!ok) break;
+          nvfp4_tile(kbuf(st), kscl(st), L - tile * kTileRows, ct);
+          fence_proxy_async_smem();
+          mbar_arrive(&b.k_ready[st]);
+        }
         // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
         ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
              mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
         if (!ok) break;
-        if constexpr (Fmt<FMT>::NARROW) {
+        if constexpr (Fmt<FMT>::SCALED) {
+          nvfp4_tile(vbuf(st), vscl(st), L - tile * kTileRows, ct);
+        } else if constexpr (Fmt<FMT>::NARROW) {
           // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
           // this role converts chunks ct, ct + CVT_THREADS, ...; without a
           // converter warpgroup the softmax warpgroups convert the others
@@ -416,6 +495,24 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           }
           return pg;
         };
+        // nvfp4: the 8-byte scale rows of this tile's valid rows (rows lane +
+        // 32 i), K or V, into the stage (rows past the sequence are left
+        // stale: the converter zeroes those rows); each lane then arrives once
+        // per full barrier, when its copies have landed
+        auto copy_scales = [&](int tile, int pg, int st, bool v) {
+          const int valid = L - tile * kTileRows;
+          const unsigned char* base = reinterpret_cast<const unsigned char*>(v ? a.v_scales : a.k_scales);
+          const int64_t sp = v ? a.vs_stride_page : a.ks_stride_page, sr = v ? a.vs_stride_row : a.ks_stride_row;
+          const int64_t sh = v ? a.vs_stride_head : a.ks_stride_head;
+          unsigned char* dst = v ? vscl(st) : kscl(st);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = lane + 32 * i;
+            const int pr = __shfl_sync(0xffffffffu, pg, r / PS);
+            if (r < valid && pr < a.num_pages)
+              cp_async8(dst + r * 8, base + (int64_t)pr * sp + (int64_t)(r % PS) * sr + (int64_t)h * sh);
+          }
+        };
         int pg_next = page_coord(tb);
         for (int tile = tb; tile < te; ++tile, ++it) {
           const int st = it % S;
@@ -429,6 +526,11 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * C::K_TX);
             __syncwarp();
             if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h);
+            if constexpr (Fmt<FMT>::SCALED) {
+              copy_scales(tile, pg, st, false);
+              copy_scales(tile, pg, st, true);
+              cp_async_arrive_noinc(&b.k_full[st]);
+            }
             k_issued = it + 1;
             continue;
           }
@@ -438,6 +540,10 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], C::K_TX);
           __syncwarp();
           if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg);
+          if constexpr (Fmt<FMT>::SCALED) {
+            copy_scales(tile, pg, st, false);
+            cp_async_arrive_noinc(&b.k_full[st]);
+          }
           k_issued = it + 1;
           if (lane == 0) ok = mbar_wait(&b.v_empty[st], par, abort_flag, MJ_TC_WAIT_NS);
           ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -445,6 +551,10 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], C::K_TX);
           __syncwarp();
           if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg);
+          if constexpr (Fmt<FMT>::SCALED) {
+            copy_scales(tile, pg, st, true);
+            cp_async_arrive_noinc(&b.v_full[st]);
+          }
           v_issued = it + 1;
         }
       }
@@ -499,7 +609,8 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           const int n = te - tb;
           for (int i = 0; ok && i < n; ++i, ++it) {  // S_i = K_i . Q^T, then PV of the tile before
             const int st = it % S;
-            ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+            // nvfp4: K converted to e4m3 (k_ready) rather than landed (k_full)
+            ok = mbar_wait(Fmt<FMT>::SCALED ? &b.k_ready[st] : &b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
                  mbar_wait(&b.s_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
             if (!ok) break;
             tc_fence_after();
@@ -970,7 +1081,12 @@ static EncodeTiledFn encode_fn() {
 
 // Why the tensor-core kernel cannot run these arguments (nullptr = it can).
 const char* tc_ineligible(const mj_decode_args& a) {
-  if (a.kv_format == MJ_KV_NVFP4) return "nvfp4 runs on the CUDA-core kernel";
+  if (a.kv_format == MJ_KV_NVFP4) {  // the scale rows arrive by 8-byte copies
+    if (!a.k_scales || !a.v_scales || (uintptr_t)a.k_scales % 8 || (uintptr_t)a.v_scales % 8) return "nvfp4 scale alignment";
+    const int64_t ss[6] = {a.ks_stride_page, a.ks_stride_row, a.ks_stride_head, a.vs_stride_page, a.vs_stride_row, a.vs_stride_head};
+    for (int i = 0; i < 6; ++i)
+      if (ss[i] % 8) return "nvfp4 scale stride alignment";
+  }
   if (a.head_size != 128) return "head_size != 128";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";
@@ -988,7 +1104,7 @@ const char* tc_ineligible(const mj_decode_args& a) {
 // packed bytes, 4 padding), 4-bit codes 16 per 16-byte slot (8 and 8).
 static CUtensorMapDataType tma_type(int kv_format) {
   if (kv_format == MJ_KV_E2M3 || kv_format == MJ_KV_E3M2) return CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B;
-  if (kv_format == MJ_KV_E2M1) return CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;
+  if (kv_format == MJ_KV_E2M1 || kv_format == MJ_KV_NVFP4) return CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B;
   return CU_TENSOR_MAP_DATA_TYPE_UINT8;
 }
 
@@ -1108,15 +1224,22 @@ static cudaError_t launch_one_wg(const mj_decode_args& a, const CUtensorMap& mk,
 template <int FMT, bool FUSED>
 static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
                                 cudaStream_t stream) {
-  if (n_q <= 4) return launch_one_wg<FMT, 4, FUSED>(a, mk, mv, stream);
-  if (n_q <= 8) return launch_one_wg<FMT, 8, FUSED>(a, mk, mv, stream);
-  if (n_q <= 16) return launch_one_wg<FMT, 16, FUSED>(a, mk, mv, stream);
-  if (n_q <= 32) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
-  cudaError_t e = cudaErrorNotSupported;
-  if constexpr (tc::Fmt<FMT>::NARROW) e = launch_tc_t<FMT, 16, 3, 1, FUSED>(a, mk, mv, stream);
-  if (e == cudaErrorNotSupported) e = launch_tc_t<FMT, 16, 3, 0, FUSED>(a, mk, mv, stream);
-  if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
-  return e;
+  if constexpr (tc::Fmt<FMT>::SCALED) {  // nvfp4: the variants with a converter warpgroup only
+    if (n_q <= 4) return launch_tc_t<FMT, 4, 1, 1, FUSED>(a, mk, mv, stream);
+    if (n_q <= 8) return launch_tc_t<FMT, 8, 1, 1, FUSED>(a, mk, mv, stream);
+    if (n_q <= 16) return launch_tc_t<FMT, 16, 1, 1, FUSED>(a, mk, mv, stream);
+    return launch_tc_t<FMT, 16, 3, 1, FUSED>(a, mk, mv, stream);
+  } else {
+    if (n_q <= 4) return launch_one_wg<FMT, 4, FUSED>(a, mk, mv, stream);
+    if (n_q <= 8) return launch_one_wg<FMT, 8, FUSED>(a, mk, mv, stream);
+    if (n_q <= 16) return launch_one_wg<FMT, 16, FUSED>(a, mk, mv, stream);
+    if (n_q <= 32) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
+    cudaError_t e = cudaErrorNotSupported;
+    if constexpr (tc::Fmt<FMT>::NARROW) e = launch_tc_t<FMT, 16, 3, 1, FUSED>(a, mk, mv, stream);
+    if (e == cudaErrorNotSupported) e = launch_tc_t<FMT, 16, 3, 0, FUSED>(a, mk, mv, stream);
+    if (e == cudaErrorNotSupported) return launch_tc_t<FMT, 16, 2, 0, FUSED>(a, mk, mv, stream);
+    return e;
+  }
 }
 
 template <bool FUSED>
@@ -1126,6 +1249,7 @@ static cudaError_t dispatch_nq(const mj_decode_args& a, int n_q, const CUtensorM
     case MJ_KV_E2M3: return dispatch_fmt<MJ_KV_E2M3, FUSED>(a, n_q, mk, mv, stream);
     case MJ_KV_E3M2: return dispatch_fmt<MJ_KV_E3M2, FUSED>(a, n_q, mk, mv, stream);
     case MJ_KV_E2M1: return dispatch_fmt<MJ_KV_E2M1, FUSED>(a, n_q, mk, mv, stream);
+    case MJ_KV_NVFP4: return dispatch_fmt<MJ_KV_NVFP4, FUSED>(a, n_q, mk, mv, stream);
     default: return dispatch_fmt<MJ_KV_FP8_E4M3, FUSED>(a, n_q, mk, mv, stream);
   }
 }
@@ -1147,8 +1271,12 @@ cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool*
   }
   *handled = true;
   const int n_q = a.q_len * (a.h_q / a.h_k);
-  if (fused) return dispatch_nq<true>(a, n_q, mk, mv, stream);
-  return dispatch_nq<false>(a, n_q, mk, mv, stream);
+  const cudaError_t e = fused ? dispatch_nq<true>(a, n_q, mk, mv, stream) : dispatch_nq<false>(a, n_q, mk, mv, stream);
+  if (e == cudaErrorNotSupported) {  // no variant's register split fits this device: the CUDA-core kernel runs
+    *handled = false;
+    return cudaSuccess;
+  }
+  return e;
 }
 
 }  // namespace mj

@@ -155,15 +155,25 @@ def _kernel_of(c, **kw):
 
 
 @pytest.mark.parametrize("kernel", ["simt", "auto"])
-@pytest.mark.parametrize("layout", ["BHN2D", "B2NHD", "BHN2R"])
-@pytest.mark.parametrize("q_len,h_q", [(1, 16), (1, 64), (3, 32)])
+@pytest.mark.parametrize("layout", ["BHN2D", "B2NHD", "BHN2R", "2BHND"])
+@pytest.mark.parametrize("q_len,h_q", [(1, 16), (1, 32), (1, 64), (3, 32), (8, 32)])
 def test_decode_matches_oracle(kernel, layout, q_len, h_q):
     """Decode over an nvfp4 cache (descale gs * 2^3, per tensor as the
     reference harness passes it) against the fp32 oracle on the kernel values."""
     c = Case(seq_lens=(700, 1, 2049, 130, 33), q_len=q_len, h_q=h_q, h_k=4, kv_format="nvfp4", layout=layout,
              seed=13)
     kname = _kernel_of(c, kernel=kernel)
-    assert kname == "decode_simt" or kernel == "auto"
+    assert kname == ("decode_simt" if kernel == "simt" else "decode_tc")
+    # rows past each sequence's end inside its last page: NaN scale bytes and
+    # the largest codes, which no kernel may let into the output
+    for s, L in enumerate(c.seq_lens):
+        blk, off = divmod(L, c.PS)
+        if off:
+            page = int(c.block_table_cpu[s, blk])
+            for t in (c.k_scales, c.v_scales):
+                t[page, off:] = 0x7F
+            for t in (c.k_view, c.v_view):
+                t[page, off:] = 0x77
     out, _, _ = c.run(kernel=kernel)
     ref, _ = c.oracle()
     T = c.b * c.q_len
