@@ -1,6 +1,6 @@
 """Decode-attention benchmark (the BASELINE.json metric): KV GB/s and us/step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg5] [--kv fp8|e2m3|e3m2|e2m1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg5] [--kv fp8|e2m3|e3m2|e2m1|nvfp4]
     python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
     python bench.py --impl reference ...   # the reference's CPU path (oracle port)
 
@@ -64,11 +64,13 @@ VMAX = {"e2m3": 7.5, "e3m2": 28.0, "e2m1": 6.0}  # largest code value of each na
 
 
 def row_bytes(d, kv):
-    return {"fp8": d, "e2m3": d * 3 // 4, "e3m2": d * 3 // 4, "e2m1": d // 2}[kv]
+    """Packed code bytes of one K (or V) row."""
+    return {"fp8": d, "e2m3": d * 3 // 4, "e3m2": d * 3 // 4, "e2m1": d // 2, "nvfp4": d // 2}[kv]
 
 
 def kv_bytes(lens, h_k, d, kv):
-    return int(sum(lens)) * h_k * 2 * row_bytes(d, kv)
+    """KV bytes a decode step streams (nvfp4 rows carry d / 16 scale bytes)."""
+    return int(sum(lens)) * h_k * 2 * (row_bytes(d, kv) + (d // 16 if kv == "nvfp4" else 0))
 
 
 class Workload:
@@ -108,6 +110,12 @@ class Workload:
         # the vLLM-main / reference layout (B, H, N, 2*row): K|V cell per (page, head, slot)
         self.kv_cache = torch.empty(self.num_pages, h_k, PS, 2 * rb, dtype=torch.uint8, device=device)
         self.k_view, self.v_view = split_kv_cache(self.kv_cache, "BHN2D", rb)
+        self.k_scales = self.v_scales = None
+        if self.fmt == "nvfp4":
+            # group scales (page, head, slot, K|V, d / 16): a page's rows of one head are contiguous
+            self.scale_cache = torch.empty(self.num_pages, h_k, PS, 2, d // 16, dtype=torch.uint8, device=device)
+            self.k_scales = self.scale_cache[:, :, :, 0].transpose(1, 2)
+            self.v_scales = self.scale_cache[:, :, :, 1].transpose(1, 2)
         outliers = 0.01 if name == "cfg3" else 0.0
 
         def gen(n):
@@ -121,6 +129,9 @@ class Workload:
         # no headroom)
         if self.fmt == "fp8":
             self.k_scale = self.v_scale = torch.ones(1, device=device)
+        elif self.fmt == "nvfp4":  # one global scale per tensor: amax / (6 * 448) (quant.py:74)
+            self.k_scale = (gen(1 << 20).float().abs().amax().clamp(min=1e-12) / 2688.0).reshape(1)
+            self.v_scale = (gen(1 << 20).float().abs().amax().clamp(min=1e-12) / 2688.0).reshape(1)
         else:
             smp = gen(1 << 20).float()
             self.k_scale = (smp.abs().amax(0).clamp(min=1e-6) / VMAX[self.fmt]).contiguous()
@@ -132,10 +143,14 @@ class Workload:
         for t0 in range(0, total, chunk):
             n = min(chunk, total - t0)
             slots = torch.arange(t0, t0 + n, dtype=torch.int64, device=device)
-            kvfp6.reshape_and_cache(gen(n), gen(n), self.k_view, self.v_view, slots, self.k_scale, self.v_scale, self.fmt)
+            kvfp6.reshape_and_cache(gen(n), gen(n), self.k_view, self.v_view, slots, self.k_scale, self.v_scale, self.fmt,
+                                    k_scales=self.k_scales, v_scales=self.v_scales)
         torch.cuda.synchronize(device)
         h_r = self.h_q // self.h_k
-        if self.fmt != "fp8":
+        if self.fmt == "nvfp4":  # descale gs * 2^3 (the converted values carry 2^-3)
+            self.q_mul = self.o_mul = None
+            self.kd, self.vd = self.k_scale * 8.0, self.v_scale * 8.0
+        elif self.fmt != "fp8":
             self.q_mul = self.k_scale.repeat_interleave(h_r, 0).contiguous()
             self.o_mul = self.v_scale.repeat_interleave(h_r, 0).contiguous()
             self.kd = self.vd = torch.ones(1, device=device)
@@ -300,13 +315,17 @@ def cpu_reference_step(name, kv, world, n_seqs=1, seed=1234):
     rb = row_bytes(d, w["kv"])
     kb = rng.integers(0, 256, size=(pages, PS, h_k, rb), dtype=np.uint8)
     vb = rng.integers(0, 256, size=(pages, PS, h_k, rb), dtype=np.uint8)
+    ks = vs = None
     if w["kv"] == "fp8":  # no NaN codes in a real cache
         kb[(kb & 0x7F) == 0x7F] = 0
         vb[(vb & 0x7F) == 0x7F] = 0
+    if w["kv"] == "nvfp4":  # group scale bytes, no NaN
+        ks = rng.integers(0, 0x7F, size=(pages, PS, h_k, d // 16), dtype=np.uint8)
+        vs = rng.integers(0, 0x7F, size=(pages, PS, h_k, d // 16), dtype=np.uint8)
     q = torch.from_numpy(rng.standard_normal((len(lens) * ql, h_q, d)).astype(np.float32)).to(torch.bfloat16)
     t0 = time.perf_counter()
-    kvals = attention.dequant_pool(kb, w["kv"], d)
-    vvals = attention.dequant_pool(vb, w["kv"], d)
+    kvals = attention.dequant_pool(kb, w["kv"], d, ks)
+    vvals = attention.dequant_pool(vb, w["kv"], d, vs)
     attention.decode_attention(q, kvals, vvals, btab, lens, len(lens), ql, 1.0 / math.sqrt(d))
     dt = time.perf_counter() - t0
     return dt, kv_bytes(lens, h_k, d, w["kv"])
@@ -346,7 +365,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
-    ap.add_argument("--kv", default=None, choices=[None, "fp8", "e2m3", "e3m2", "e2m1"])
+    ap.add_argument("--kv", default=None, choices=[None, "fp8", "e2m3", "e3m2", "e2m1", "nvfp4"])
     ap.add_argument("--page-size", type=int, default=None, help="override the workload's KV page size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -371,9 +390,10 @@ def main():
 
     wl = Workload(args.workload, args.kv, rank, world, dev, page_size=args.page_size)
     stream = _stream(dev)
-    cw = kvfp6.cache_write_args(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt)
+    cw = kvfp6.cache_write_args(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt,
+                                k_scales=wl.k_scales, v_scales=wl.v_scales)
     da = wl.runner.decode_args(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale,
-                               q_mul=wl.q_mul, o_mul=wl.o_mul)
+                               q_mul=wl.q_mul, o_mul=wl.o_mul, k_scales=wl.k_scales, v_scales=wl.v_scales)
     da.with_combine = 0
     combine = wl.plan.with_reduction and not wl.runner.merges_in_kernel(da)
     if world > 1:
@@ -439,8 +459,10 @@ def main():
         wl.query.copy_(q_h, non_blocking=True)
         wl.new_k.copy_(k_h, non_blocking=True)
         wl.new_v.copy_(v_h, non_blocking=True)
-        kvfp6.reshape_and_cache(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt)
-        wl.runner.run(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale, q_mul=wl.q_mul, o_mul=wl.o_mul)
+        kvfp6.reshape_and_cache(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt,
+                                k_scales=wl.k_scales, v_scales=wl.v_scales)
+        wl.runner.run(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale, q_mul=wl.q_mul, o_mul=wl.o_mul,
+                      k_scales=wl.k_scales, v_scales=wl.v_scales)
         if world > 1:
             gather_heads(local_out, world, buf=gbuf, out=full_out)
             o_h.copy_(full_out.view(wl.T, -1), non_blocking=True)

@@ -103,47 +103,26 @@ __device__ __forceinline__ uint4 e2m1x16_to_e4m3(uint4 raw) {
                     e2m1_bytes(__byte_perm(e1, o1, 0x5140)), e2m1_bytes(__byte_perm(e1, o1, 0x7362)));
 }
 
-// nvfp4: 16 e2m1 codes (the first 8 bytes of a 16U4 slot, low nibble first)
-// of one scale group -> 16 e4m3 bytes e4m3(value(code) * scale * 2^-3).
-// s2 holds scale * 2^-3 in both f16 halves. value(code) (<= 2 significant
-// bits) times an e4m3 scale (<= 4) is exact in f16, as is the 2^-3, so the one
-// rounding is the e4m3 conversion (nearest even) -- the reference's fp32
-// arithmetic (quant.py:81-83) gives the same bytes.
-__device__ __forceinline__ uint4 nvfp4x16_to_e4m3(uint4 raw, uint32_t s2) {
-  uint4 o;
-  asm("{\n\t.reg .b8 b0, b1, b2, b3, b4, b5, b6, b7;\n\t"
-      ".reg .b32 h0, h1, h2, h3, h4, h5, h6, h7;\n\t"
-      ".reg .b16 e0, e1, e2, e3, e4, e5, e6, e7;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "mov.b32 {b4, b5, b6, b7}, %5;\n\t"
-      "cvt.rn.f16x2.e2m1x2 h0, b0;\n\tcvt.rn.f16x2.e2m1x2 h1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 h2, b2;\n\tcvt.rn.f16x2.e2m1x2 h3, b3;\n\t"
-      "cvt.rn.f16x2.e2m1x2 h4, b4;\n\tcvt.rn.f16x2.e2m1x2 h5, b5;\n\t"
-      "cvt.rn.f16x2.e2m1x2 h6, b6;\n\tcvt.rn.f16x2.e2m1x2 h7, b7;\n\t"
-      "mul.rn.f16x2 h0, h0, %6;\n\tmul.rn.f16x2 h1, h1, %6;\n\t"
-      "mul.rn.f16x2 h2, h2, %6;\n\tmul.rn.f16x2 h3, h3, %6;\n\t"
-      "mul.rn.f16x2 h4, h4, %6;\n\tmul.rn.f16x2 h5, h5, %6;\n\t"
-      "mul.rn.f16x2 h6, h6, %6;\n\tmul.rn.f16x2 h7, h7, %6;\n\t"
-      "cvt.rn.satfinite.e4m3x2.f16x2 e0, h0;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e1, h1;\n\t"
-      "cvt.rn.satfinite.e4m3x2.f16x2 e2, h2;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e3, h3;\n\t"
-      "cvt.rn.satfinite.e4m3x2.f16x2 e4, h4;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e5, h5;\n\t"
-      "cvt.rn.satfinite.e4m3x2.f16x2 e6, h6;\n\tcvt.rn.satfinite.e4m3x2.f16x2 e7, h7;\n\t"
-      "mov.b32 %0, {e0, e1};\n\tmov.b32 %1, {e2, e3};\n\t"
-      "mov.b32 %2, {e4, e5};\n\tmov.b32 %3, {e6, e7};\n\t}"
-      : "=r"(o.x), "=r"(o.y), "=r"(o.z), "=r"(o.w)
-      : "r"(raw.x), "r"(raw.y), "r"(s2));
-  return o;
+// nvfp4: 8 e2m1 codes (nibbles of w, code 0 lowest) -> 8 e4m3 bytes
+// e4m3(value(code) * scale * 2^-3), given t = the 8 bytes e4m3(value(m) *
+// scale * 2^-3) of the group's scale for magnitudes m = 0..7 (built once per
+// CTA for every scale byte). The magnitude bytes come from one byte permute
+// per 4 codes; the signs from a permute in sign-replicate mode (a selector
+// nibble with bit 3 set copies the msb of the chosen byte over the output
+// byte): code 2i's sign is the msb of byte i of w << 4, code 2i+1's of byte i
+// of w. e4m3 rounding is symmetric in the sign, so this is the same byte.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
 }
-
-// scale byte -> f16x2 (scale * 2^-3, both halves); a NaN byte (never written
-// by the quantizer, possible in unwritten rows) reads as 0
-__device__ __forceinline__ uint32_t nvfp4_scale2(uint32_t sb) {
-  sb = (sb & 0x7Fu) == 0x7Fu ? 0u : sb;
-  uint32_t h;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((unsigned short)(sb | (sb << 8))));
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x30003000u));  // x 2^-3
-  return r;
+__device__ __forceinline__ uint2 nvfp4x8_to_e4m3(uint32_t w, uint2 t) {
+  const uint32_t mag_lo = prmt(t.x, t.y, w & 0x7777u);
+  const uint32_t mag_hi = prmt(t.x, t.y, (w >> 16) & 0x7777u);
+  const uint32_t a = w << 4;
+  const uint32_t sg_lo = prmt(a, w, 0xD9C8u);  // msb of a.b0, w.b0, a.b1, w.b1
+  const uint32_t sg_hi = prmt(a, w, 0xFBEAu);  // msb of a.b2, w.b2, a.b3, w.b3
+  return make_uint2(mag_lo | (sg_lo & 0x80808080u), mag_hi | (sg_hi & 0x80808080u));
 }
 
 // Per-format constants of the tensor-core path.
@@ -212,7 +191,9 @@ struct Cfg {
   // nvfp4: per stage the K then V scale rows of the tile ([128 rows][8 B] each)
   static constexpr int SC_OFF = (MISC_OFF + 64 + NWG * 4 * 4 * NQP + 15) / 16 * 16;
   static constexpr int SC_BYTES = Fmt<FMT>::SCALED ? STAGES * 2 * 128 * 8 : 0;
-  static constexpr int SMEM = SC_OFF + SC_BYTES;
+  // nvfp4: for each of the 256 scale bytes the e4m3 bytes of the 8 code magnitudes
+  static constexpr int LUT_OFF = SC_OFF + SC_BYTES;
+  static constexpr int SMEM = LUT_OFF + (Fmt<FMT>::SCALED ? 256 * 8 : 0);
 };
 
 struct Bars {
@@ -341,7 +322,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       mbar_init(&b.k_empty[i], 1);
       mbar_init(&b.v_full[i], FULL);
       mbar_init(&b.v_empty[i], 1);  // released by the PV MMA
-      mbar_init(&b.k_ready[i], C::CVT_ROLE);
+      mbar_init(&b.k_ready[i], C::CVT_ROLE - 64);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&b.s_full[i], 1);
@@ -349,8 +330,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       mbar_init(&b.p_full[i], 128 * NWG);
       mbar_init(&b.o_full[i], 1);
       if (i == 0) mbar_init(b.o_free, 128 * NWG);
-      // e2m3: converter warps and softmax warpgroups share the V conversion
-      mbar_init(&b.v_ready[i], Fmt<FMT>::NARROW ? C::CVT_THREADS : C::CVT_ROLE);
+      // e2m3: converter warps and softmax warpgroups share the V conversion;
+      // nvfp4: warps 2-3 convert V (the converter warpgroup converts K)
+      mbar_init(&b.v_ready[i], Fmt<FMT>::SCALED ? 64 : Fmt<FMT>::NARROW ? C::CVT_THREADS : C::CVT_ROLE);
       mbar_init(&b.v_free[i], 1);
       mbar_init(&b.q_full[i], NWG);
     }
@@ -358,6 +340,23 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
     *abort_flag = 0;
     never_abort = 0;
     fence_mbar_init();
+  }
+  if constexpr (Fmt<FMT>::SCALED) {
+    // e4m3(value(m) * scale * 2^-3) for every scale byte and magnitude m
+    // (quant.py:81-83: an exact fp32 product, one rounding); a NaN scale byte,
+    // which the quantizer never writes, gives zeros
+    uint2* lut = reinterpret_cast<uint2*>(sm + C::LUT_OFF);
+    for (int e = threadIdx.x; e < 256; e += blockDim.x) {
+      uint32_t lo = 0, hi = 0;
+      if ((e & 0x7F) != 0x7F) {
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          lo |= (uint32_t)nvfp4_byte((uint32_t)m, (uint8_t)e) << (8 * m);
+          hi |= (uint32_t)nvfp4_byte((uint32_t)(m + 4), (uint8_t)e) << (8 * m);
+        }
+      }
+      lut[e] = make_uint2(lo, hi);
+    }
   }
   if (warp == kWarpTma && lane == 0) {
     prefetch_tmap(&tmk);
@@ -408,13 +407,20 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   // takes chunks ct, ct + CVT_ROLE, ...): the 16 codes of a 16U4 slot are one
   // scale group, whose logical index within the row is the slot's swizzled
   // position XOR the row (mod 8); rows at or past `valid` become zeros.
-  auto nvfp4_tile = [&](unsigned char* buf, const unsigned char* scl, int valid, int ct) {
+  auto nvfp4_tile = [&](unsigned char* buf, const unsigned char* scl, int valid, int ct, int nthr) {
+    const uint2* lut = reinterpret_cast<const uint2*>(sm + C::LUT_OFF);
 #pragma unroll 2
-    for (int c = ct; c < kTileBytes / 16; c += C::CVT_ROLE) {
+    for (int c = ct; c < kTileBytes / 16; c += nthr) {
       const int r = c >> 3;
       uint4* q = reinterpret_cast<uint4*>(buf + vchunk(c));
-      if (r < valid) *q = nvfp4x16_to_e4m3(*q, nvfp4_scale2(scl[r * 8 + ((c ^ r) & 7)]));
-      else *q = make_uint4(0, 0, 0, 0);
+      if (r < valid) {
+        const uint2 t = lut[scl[r * 8 + ((c ^ r) & 7)]];
+        const uint4 raw = *q;
+        const uint2 o0 = nvfp4x8_to_e4m3(raw.x, t), o1 = nvfp4x8_to_e4m3(raw.y, t);
+        *q = make_uint4(o0.x, o0.y, o1.x, o1.y);
+      } else {
+        *q = make_uint4(0, 0, 0, 0);
+      }
     }
   };
 
@@ -428,20 +434,33 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       const int L = a.seq_lens[seq];
       for (int tile = tb; tile < te; ++tile, ++it) {
         const int st = it % S;
-        if constexpr (Fmt<FMT>::SCALED) {  // K first: the S MMA waits for it (k_ready)
-          ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS);
-          if (!ok) break;
-          nvfp4_tile(kbuf(st), kscl(st), L - tile * kTileRows, ct);
-          fence_proxy_async_smem();
-          mbar_arrive(&b.k_ready[st]);
+        if constexpr (Fmt<FMT>::SCALED) {
+          // two converters: the converter warpgroup (ct >= 64) takes K, which
+          // the S MMA waits for, so it never queues behind a V tile; warps 2-3
+          // take V (needed only by the PV MMA; v_free keeps them at most two
+          // tiles ahead of it)
+          const int valid = L - tile * kTileRows;
+          if (ct >= 64) {
+            ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS);
+            if (!ok) break;
+            nvfp4_tile(kbuf(st), kscl(st), valid, ct - 64, C::CVT_ROLE - 64);
+            fence_proxy_async_smem();
+            mbar_arrive(&b.k_ready[st]);
+          } else {
+            ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
+                 mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
+            if (!ok) break;
+            nvfp4_tile(vbuf(st), vscl(st), valid, ct, 64);
+            fence_proxy_async_smem();
+            mbar_arrive(&b.v_ready[it & 1]);
+          }
+          continue;
         }
         // v_free keeps this role at most two tiles ahead of the PV MMA (v_ready is a pair)
         ok = mbar_wait(FUSED ? &b.k_full[st] : &b.v_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
              mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
         if (!ok) break;
-        if constexpr (Fmt<FMT>::SCALED) {
-          nvfp4_tile(vbuf(st), vscl(st), L - tile * kTileRows, ct);
-        } else if constexpr (Fmt<FMT>::NARROW) {
+        if constexpr (Fmt<FMT>::NARROW) {
           // in place: the 16 e4m3 bytes of a 16-code group take its 16-byte slot;
           // this role converts chunks ct, ct + CVT_THREADS, ...; without a
           // converter warpgroup the softmax warpgroups convert the others
@@ -578,12 +597,12 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         int jo = 0;  // jobs whose O accumulation has started
         // O^T += V_t^T . P_t^T for global tile t; the first tile of a job starts
         // the accumulator fresh, once the previous job's O has been read out
-        auto pv = [&](int t, bool first) {
+        auto pv_ready = [&](int t, bool first) {  // non-blocking: may PV_t be issued now?
+          return (!first || mbar_test(b.o_free, (jo & 1) ^ 1)) && mbar_test(&b.p_full[t & 1], (t >> 1) & 1) &&
+                 mbar_test(&b.v_ready[t & 1], (t >> 1) & 1);
+        };
+        auto pv = [&](int t, bool first) {  // issue PV_t (its barriers have completed)
           const int st = t % S;
-          if (first && !mbar_wait(b.o_free, (jo & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS)) return false;
-          if (!(mbar_wait(&b.p_full[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-                mbar_wait(&b.v_ready[t & 1], (t >> 1) & 1, abort_flag, MJ_TC_WAIT_NS)))
-            return false;
           if (first) ++jo;
           tc_fence_after();
           const uint32_t vaddr = smem_addr(vbuf(st));
@@ -598,7 +617,6 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           mma_commit(&b.o_full[t & 1]);
           mma_commit(&b.v_empty[st]);
           mma_commit(&b.v_free[t & 1]);
-          return true;
         };
         for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
           int seq, tb, te, split, h, g;
@@ -607,24 +625,48 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           const uint32_t qaddr = smem_addr(qbuf(jc & 1));
           ++jc;
           const int n = te - tb;
-          for (int i = 0; ok && i < n; ++i, ++it) {  // S_i = K_i . Q^T, then PV of the tile before
-            const int st = it % S;
-            // nvfp4: K converted to e4m3 (k_ready) rather than landed (k_full)
-            ok = mbar_wait(Fmt<FMT>::SCALED ? &b.k_ready[st] : &b.k_full[st], (it / S) & 1, abort_flag, MJ_TC_WAIT_NS) &&
-                 mbar_wait(&b.s_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, MJ_TC_WAIT_NS);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t kaddr = smem_addr(kbuf(st));
-            const uint32_t d = tmem + (uint32_t)((it & 1) * NS);
+          // Issue S_i = K_i . Q^T and PV_j in whichever order their inputs
+          // become ready: S first when both are, but PV_j does not wait behind
+          // a K tile still in flight (its stage frees only after PV_j). S_i
+          // goes out only after PV_{i-2}, so a landed S_t still means PV_{t-2}
+          // is complete (the softmax reuses P buffers on that).
+          const int base = it;
+          int si = 0, pj = 0;
+          uint64_t idle_since = 0;
+          while (ok && pj < n) {
+            bool moved = false;
+            if (ok && si < n && pj >= si - 1) {
+              const int t = base + si, st = t % S;
+              // nvfp4: K converted to e4m3 (k_ready) rather than landed (k_full)
+              if (mbar_test(Fmt<FMT>::SCALED ? &b.k_ready[st] : &b.k_full[st], (t / S) & 1) &&
+                  mbar_test(&b.s_free[t & 1], ((t >> 1) & 1) ^ 1)) {
+                tc_fence_after();
+                const uint32_t kaddr = smem_addr(kbuf(st));
+                const uint32_t d = tmem + (uint32_t)((t & 1) * NS);
   #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
-                         idesc_s, k > 0);
-            mma_commit(&b.s_full[it & 1]);
-            if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
-            if (i >= 1) ok = pv(it - 1, i == 1);
+                for (int k = 0; k < 4; ++k)
+                  mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qaddr + 32 * k, 16, 1024),
+                             idesc_s, k > 0);
+                mma_commit(&b.s_full[t & 1]);
+                if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
+                ++si;
+                moved = true;
+              }
+            }
+            if (pj < si && pv_ready(base + pj, pj == 0)) {
+              pv(base + pj, pj == 0);
+              ++pj;
+              moved = true;
+            }
+            if (moved) {
+              idle_since = 0;
+            } else {  // bounded: the same limit as every other wait
+              const uint64_t now = globaltimer();
+              if (!idle_since) idle_since = now;
+              if (*abort_flag || now - idle_since > MJ_TC_WAIT_NS) ok = false;
+            }
           }
-          if (ok) ok = pv(it - 1, n == 1);  // the job's last tile
+          it = base + n;
         }
         if (!ok && !*abort_flag) give_up();
         mma_commit(b.drain);  // all issued MMAs complete before TMEM is released

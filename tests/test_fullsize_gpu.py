@@ -32,8 +32,12 @@ def _sampled_reference(wl, seqs, heads):
         for h in heads:
             kb = wl.k_view[pages.to(wl.k_view.device)][:, :, h : h + 1].cpu()
             vb = wl.v_view[pages.to(wl.v_view.device)][:, :, h : h + 1].cpu()
-            kv = dequant_pool(kb, wl.fmt, d)
-            vv = dequant_pool(vb, wl.fmt, d)
+            ks = vs = None
+            if wl.fmt == "nvfp4":
+                ks = wl.k_scales[pages.to(wl.k_scales.device)][:, :, h : h + 1].cpu()
+                vs = wl.v_scales[pages.to(wl.v_scales.device)][:, :, h : h + 1].cpu()
+            kv = dequant_pool(kb, wl.fmt, d, ks)
+            vv = dequant_pool(vb, wl.fmt, d, vs)
             q = wl.query[s * ql : (s + 1) * ql, h * h_r : (h + 1) * h_r].cpu()
             qm = None if wl.q_mul is None else wl.q_mul[h * h_r : (h + 1) * h_r].cpu()
             om = None if wl.o_mul is None else wl.o_mul[h * h_r : (h + 1) * h_r].cpu()
@@ -46,7 +50,7 @@ def _sampled_reference(wl, seqs, heads):
 
 
 @pytest.mark.parametrize("workload,kv", [("cfg2", "fp8"), ("cfg3", "e2m3"), ("ns", "e2m3"), ("cfg4", "e2m3"),
-                                         ("cfg5", "e2m3"), ("cfg5", "fp8"), ("ns", "e3m2"), ("ns", "e2m1")])
+                                         ("cfg5", "e2m3"), ("cfg5", "fp8"), ("ns", "e3m2"), ("ns", "e2m1"), ("ns", "nvfp4")])
 def test_full_size_step_sampled_parity(workload, kv):
     import bench
 
@@ -65,8 +69,10 @@ def _check(wl, workload, kv):
 
     outs = []
     for _ in range(2):
-        kvfp6.reshape_and_cache(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt)
-        wl.runner.run(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale,
+        kvfp6.reshape_and_cache(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt,
+                                k_scales=wl.k_scales, v_scales=wl.v_scales)
+        wl.runner.run(wl.plan, wl.query, wl.out, wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale, k_scales=wl.k_scales,
+                      v_scales=wl.v_scales,
                       q_mul=wl.q_mul, o_mul=wl.o_mul)
         torch.cuda.synchronize()
         wl.runner.check_status()
