@@ -27,7 +27,9 @@
 //   e2m3 V cannot be an MN-major MMA operand, so converter warps (a whole
 //   warpgroup in the one-warpgroup variants) rewrite each 16-code slot in
 //   place as 16 e4m3 bytes of value code * 2^-6 (exact; the 2^6 is folded
-//   into the output scale).
+//   into the output scale); e3m2 and e2m1 likewise. nvfp4 (e2m1 codes with an
+//   e4m3 scale per 16) converts K and V: each slot becomes
+//   e4m3(code * scale * 2^-3), its scale rows arriving with the stage.
 //
 // Numerics: split-fp8 Q and P carry ~12 significant bits each
 // (hi + mid / 16 + lo / 256), accumulation is fp32 in TMEM, softmax is fp32;
