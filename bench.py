@@ -76,7 +76,7 @@ def kv_bytes(lens, h_k, d, kv):
 class Workload:
     """One rank's shard of a workload, resident on the device."""
 
-    def __init__(self, name, kv, rank, world, device, seed=1234, page_size=None):
+    def __init__(self, name, kv, rank, world, device, seed=1234, page_size=None, batch=None):
         from mjolnir_b200 import kvfp6
         from mjolnir_b200.runner import DecodeRunner, split_kv_cache
 
@@ -85,6 +85,8 @@ class Workload:
             w["kv"] = kv
         if page_size:
             w["PS"] = page_size
+        if batch:  # a smaller batch of the same shape (profiling captures)
+            w["b"] = batch
         self.w, self.name = w, name
         if w["h_k"] % world:
             raise SystemExit(f"{w['h_k']} KV heads do not shard over {world} GPUs")
@@ -367,6 +369,7 @@ def main():
     ap.add_argument("--workload", default="cfg5", choices=sorted(WORKLOADS))
     ap.add_argument("--kv", default=None, choices=[None, "fp8", "e2m3", "e3m2", "e2m1", "nvfp4"])
     ap.add_argument("--page-size", type=int, default=None, help="override the workload's KV page size")
+    ap.add_argument("--batch", type=int, default=None, help="override the workload's batch (small profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -388,7 +391,7 @@ def main():
     from mjolnir_b200 import _lib, kvfp6
     from mjolnir_b200.runner import _stream
 
-    wl = Workload(args.workload, args.kv, rank, world, dev, page_size=args.page_size)
+    wl = Workload(args.workload, args.kv, rank, world, dev, page_size=args.page_size, batch=args.batch)
     stream = _stream(dev)
     cw = kvfp6.cache_write_args(wl.new_k, wl.new_v, wl.k_view, wl.v_view, wl.slots, wl.k_scale, wl.v_scale, wl.fmt,
                                 k_scales=wl.k_scales, v_scales=wl.v_scales)
