@@ -26,6 +26,18 @@ __device__ __forceinline__ void store_elem(void* p, int64_t i, int dt, float v) 
   else reinterpret_cast<float*>(p)[i] = v;
 }
 
+// warp-wide max / sum, the result in every lane
+__device__ __forceinline__ float warp_allmax(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 // max that propagates NaN (as torch's amax does)
 __device__ __forceinline__ float nan_max(float a, float b) { return (a > b || a != a) ? a : b; }
 
