@@ -499,6 +499,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       // ---------------------------------------------------------------- producer
       const int PS = a.page_size;
       const int P = kTileRows / PS;  // pages per tile; lane p < P loads page p
+      // a KV stream read by one job is evicted first; row groups of one KV
+      // head re-read it from L2, so their loads keep the normal policy
+      const uint64_t kv_policy = n_rg > 1 ? l2_policy_evict_normal() : l2_policy_evict_first();
       int it = 0, k_issued = 0, v_issued = 0;
       bool ok = true;
       for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
@@ -546,7 +549,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             if (!ok) break;
             if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * C::K_TX);
             __syncwarp();
-            if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h);
+            if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h, kv_policy);
             if constexpr (Fmt<FMT>::SCALED) {
               copy_scales(tile, pg, st, false);
               copy_scales(tile, pg, st, true);
@@ -560,7 +563,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           if (!ok) break;
           if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], C::K_TX);
           __syncwarp();
-          if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg);
+          if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg, kv_policy);
           if constexpr (Fmt<FMT>::SCALED) {
             copy_scales(tile, pg, st, false);
             cp_async_arrive_noinc(&b.k_full[st]);
@@ -571,7 +574,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           if (!ok) break;
           if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], C::K_TX);
           __syncwarp();
-          if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg);
+          if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg, kv_policy);
           if constexpr (Fmt<FMT>::SCALED) {
             copy_scales(tile, pg, st, true);
             cp_async_arrive_noinc(&b.v_full[st]);
