@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define MJ_ABI_VERSION 3
+#define MJ_ABI_VERSION 4
 
 /* status codes */
 #define MJ_OK 0
@@ -182,7 +182,9 @@ typedef struct mj_decode_args {
   int kernel;          /* MJ_KERNEL_AUTO, MJ_KERNEL_SIMT or MJ_KERNEL_TC */
   int32_t* status;     /* optional device status word (MJ_DEV_*) */
   /* Optional (num_seqs * h_k * 64) int32 counters, zero before the first
-   * call; the kernel leaves them zero again. With them, the tensor-core
+   * call; the kernel leaves them zero again -- except after a device error
+   * (a non-zero status word), when jobs may have stopped before counting
+   * in: zero them again before the next call. With them, the tensor-core
    * kernel merges the split partials itself: the last job of each (sequence,
    * KV head, row group) to finish merges them and writes the final O / LSE,
    * so no mj_combine launch is needed (mj_decode skips it). Applies to the
@@ -197,13 +199,28 @@ typedef struct mj_decode_args {
   const void* v_scales;
   int64_t ks_stride_page, ks_stride_row, ks_stride_head; /* bytes */
   int64_t vs_stride_page, vs_stride_row, vs_stride_head; /* bytes */
+  /* Limit of each wait inside the tensor-core kernel's pipeline, in ns; 0 =
+   * the built-in 0.5 s (a tile takes microseconds). A wait that runs out
+   * sets MJ_DEV_TIMEOUT in the status word; the kernel then stops, lets its
+   * copies and MMAs in flight finish, frees its tensor memory and returns,
+   * leaving the context usable (the reference's pipeline waits are
+   * unbounded). Tests shorten it to make a wait run out on purpose. */
+  uint64_t wait_limit_ns;
 } mj_decode_args;
 
 int mj_decode(const mj_decode_args* args, void* stream);
 
 /* The kernel mj_decode would launch for these arguments: MJ_KERNEL_SIMT or
- * MJ_KERNEL_TC (a negative status if the arguments are invalid). */
+ * MJ_KERNEL_TC (a negative status if the arguments are invalid). Needs the
+ * current device: the tensor-core variant is prepared (not launched) to
+ * check that it fits this build. */
 int mj_decode_kernel(const mj_decode_args* args);
+
+/* How many mj_decode calls of this process ran the CUDA-core kernel on
+ * arguments the tensor-core kernel takes, because no tensor-core variant's
+ * register split fits the build (0 on a correct build; the first such call
+ * also prints one line on stderr). */
+int mj_tc_fallbacks(void);
 
 /* LSE merge of the partials of every sequence with n_splits > 1 into O / LSE. */
 int mj_combine(const mj_decode_args* args, void* stream);
@@ -295,9 +312,11 @@ int mj_expand_pages(const mj_expand_args* args, void* stream);
  * Limit: max_splits * num_seqs * h_k * (q_len * h_q / h_k) * (head_size + 1)
  * * 4 bytes <= 16 MiB, else MJ_ERR_UNSUPPORTED with a message. The first call
  * on each device looks the array up (cudaGetSymbolAddress) -- make it before
- * any stream capture. All calls on a device share the array and it keeps the
- * last call's contents (nothing in it needs to start at zero); calls that
- * overlap on the GPU race on it and must be ordered. */
+ * any stream capture; the address found stays valid until the device or its
+ * primary context is reset (after a reset, do not call this again). All
+ * calls on a device share the array and it keeps the last call's contents
+ * (nothing in it needs to start at zero); calls that overlap on the GPU
+ * race on it and must be ordered. */
 int mj_decode_noalloc(const mj_decode_args* args, void* stream);
 
 #ifdef __cplusplus

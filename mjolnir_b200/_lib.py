@@ -48,7 +48,7 @@ MJ_SCALE_SEQ_HEAD = 3
 
 EXPORTED = ("mj_last_error", "mj_abi_version", "mj_row_bytes", "mj_cache_write", "mj_decode", "mj_combine",
             "mj_decode_noalloc", "mj_decode_kernel", "mj_expand_pages", "mj_plan_split_kv", "mj_create", "mj_plan",
-            "mj_runner_fill", "mj_runner_status", "mj_destroy")
+            "mj_runner_fill", "mj_runner_status", "mj_destroy", "mj_tc_fallbacks")
 
 _i64, _i32, _vp, _f32 = C.c_int64, C.c_int, C.c_void_p, C.c_float
 
@@ -120,6 +120,7 @@ class DecodeArgs(C.Structure):
         ("k_scales", _vp), ("v_scales", _vp),
         ("ks_stride_page", _i64), ("ks_stride_row", _i64), ("ks_stride_head", _i64),
         ("vs_stride_page", _i64), ("vs_stride_row", _i64), ("vs_stride_head", _i64),
+        ("wait_limit_ns", C.c_uint64),
     ]
 
 
@@ -158,6 +159,7 @@ def load():
             getattr(lib, fn).restype = C.c_int
         lib.mj_decode_kernel.argtypes = [C.POINTER(DecodeArgs)]
         lib.mj_decode_kernel.restype = C.c_int
+        lib.mj_tc_fallbacks.restype = C.c_int
         lib.mj_expand_pages.argtypes = [C.POINTER(ExpandArgs), _vp]
         lib.mj_expand_pages.restype = C.c_int
         _pi = C.POINTER(C.c_int32)

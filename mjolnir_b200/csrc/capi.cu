@@ -11,7 +11,7 @@ namespace mj {
 cudaError_t launch_cache_write(const mj_cache_write_args& a, cudaStream_t stream);
 cudaError_t launch_decode_simt(const mj_decode_args& a, cudaStream_t stream);
 cudaError_t launch_combine(const mj_decode_args& a, cudaStream_t stream);
-cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool* handled);
+cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool* handled, bool dry);
 const char* tc_ineligible(const mj_decode_args& a);
 cudaError_t launch_expand_pages(const mj_expand_args& a, cudaStream_t stream);
 }  // namespace mj
@@ -145,8 +145,12 @@ int mj_decode_kernel(const mj_decode_args* args) {
   if (!args) return -fail(MJ_ERR_INVALID, "mj_decode_kernel: null args");
   int rc = validate_decode(*args, "mj_decode_kernel");
   if (rc) return -rc;
-  if (args->kernel == MJ_KERNEL_SIMT) return MJ_KERNEL_SIMT;
-  return mj::tc_ineligible(*args) ? MJ_KERNEL_SIMT : MJ_KERNEL_TC;
+  if (args->kernel == MJ_KERNEL_SIMT || mj::tc_ineligible(*args)) return MJ_KERNEL_SIMT;
+  // prepare the variant mj_decode would launch, without launching it
+  bool handled = false;
+  const cudaError_t e = mj::launch_decode_tc(*args, nullptr, &handled, true);
+  if (e != cudaSuccess) return -cuda_status(e, "mj_decode_kernel (tensor-core variant)");
+  return handled ? MJ_KERNEL_TC : MJ_KERNEL_SIMT;
 }
 
 int mj_decode(const mj_decode_args* args, void* stream) {
@@ -162,7 +166,7 @@ int mj_decode(const mj_decode_args* args, void* stream) {
   bool handled = false;
   cudaError_t e = cudaSuccess;
   if (a.kernel != MJ_KERNEL_SIMT) {
-    e = mj::launch_decode_tc(a, s, &handled);
+    e = mj::launch_decode_tc(a, s, &handled, false);
     if (e != cudaSuccess) return cuda_status(e, "mj_decode launch (tensor-core kernel)");
   }
   if (!handled) {

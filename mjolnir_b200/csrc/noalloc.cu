@@ -17,7 +17,11 @@
 // Set-up: the first call on each device looks up the device address of the
 // array (cudaGetSymbolAddress with that device current) and caches it; make
 // that first call before any stream capture begins. Later calls only read
-// the cached address.
+// the cached address. The address belongs to the device's primary context
+// as it was at that first call: after cudaDeviceReset (or any reset of the
+// primary context) the module loads again, possibly elsewhere, and the
+// cached address is stale -- a process that resets a device must not call
+// this entry point on it again.
 //
 // Sharing: every call on a device uses the same array, which keeps whatever
 // the previous call left in it. Nothing needs to start at zero: the decode

@@ -5,9 +5,9 @@
 // split (arch/thor/plan.py:140-197: one wave holds sm_count * ctas_per_sm /
 // (h_k * n_q_tiles) work items; a batch smaller than a wave gets the smallest
 // chunk whose items fit one wave; items longest first, padded with empty items
-// for a fixed grid) plus the B200 rebalance (a batch that fills a wave on its
-// own picks the chunk ceil(T / k), k = 1 .. max_splits, minimising a
-// longest-first wave model plus a per-item overhead). Both produce the same
+// for a fixed grid) plus the B200 rebalance (the cheapest of that chunk and
+// every ceil(T / k), k = 1 .. max_splits, under a longest-first model of the
+// persistent grid's rounds plus a per-item overhead). Both produce the same
 // plans for the same inputs (checked against each other in the tests).
 //
 // mj_runner owns what a decode step needs besides the caller's tensors: the
@@ -88,18 +88,28 @@ int mj_plan_split_kv(const int32_t* seq_lens, int num_seqs, int h_k, int n_q_til
     T = std::max(T, tiles[b]);
   }
   const int slots = std::max(1, (sm_count * ctas_per_sm) / (h_k * n_q_tiles));
-  const int lo0 = std::max(1, ceil_div(T, max_splits));  // cap chunks per sequence
-  int chunk;
-  if (max_splits == 1) {
-    chunk = T;
-  } else if (num_seqs >= slots) {
-    chunk = T;
-    if (rebalance) {
-      std::set<int> cset;
-      for (int k = 1; k <= max_splits; ++k) cset.insert(std::max(lo0, ceil_div(T, k)));
+  const int shortest = std::max(1, ceil_div(T, max_splits));  // cap chunks per sequence
+  int chunk = T;
+  if (max_splits > 1) {
+    // the reference's chunk: none when the batch fills a round, else the
+    // shortest chunk whose items fit in one round
+    if (num_seqs < slots) {
+      int lo = shortest, hi = T;
+      while (lo < hi) {
+        const int mid = (lo + hi) / 2;
+        int64_t items = 0;
+        for (int t : tiles) items += ceil_div(t, mid);
+        if (items <= slots) hi = mid;
+        else lo = mid + 1;
+      }
+      chunk = lo;
+    }
+    if (rebalance) {  // the cheapest of it and every ceil(T / k) under the round model
+      std::set<int> cset{chunk};
+      for (int k = 1; k <= max_splits; ++k) cset.insert(std::max(shortest, ceil_div(T, k)));
       double best = 0.0;
       bool have = false;
-      for (auto it = cset.rbegin(); it != cset.rend(); ++it) {  // largest chunk first
+      for (auto it = cset.rbegin(); it != cset.rend(); ++it) {  // longest chunk first: it keeps a tie
         const double cost = wave_cost(tiles, *it, slots, item_overhead);
         if (!have || cost < best - 1e-9) {
           best = cost;
@@ -108,16 +118,6 @@ int mj_plan_split_kv(const int32_t* seq_lens, int num_seqs, int h_k, int n_q_til
         }
       }
     }
-  } else {
-    int lo = lo0, hi = T;
-    while (lo < hi) {  // smallest chunk whose total work fits one wave
-      const int mid = (lo + hi) / 2;
-      int64_t items = 0;
-      for (int t : tiles) items += ceil_div(t, mid);
-      if (items <= slots) hi = mid;
-      else lo = mid + 1;
-    }
-    chunk = lo;
   }
   std::vector<Item> work;
   for (int b = 0; b < num_seqs; ++b) {

@@ -81,12 +81,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait for the phase of `parity` to complete, giving up after `limit_ns`
-// (or at once when *abort is already set). Returns false on give-up.
+// (or at once when *abort is already set). Returns false on give-up. The
+// first test does not block, and no suspend outlasts the limit, so a short
+// limit gives up on any phase that is not already complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
+  const uint32_t hint = limit_ns < 20000u ? (uint32_t)limit_ns : 20000u;
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (mbar_try_wait_sleep(bar, parity, hint)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > limit_ns) return false;
   }

@@ -25,7 +25,7 @@ def test_header_symbols_exported():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in include/mjolnir_b200.h but not exported"
     assert set(_lib.EXPORTED) <= set(declared)
-    assert lib.mj_abi_version() == 3
+    assert lib.mj_abi_version() == 4
     assert lib.mj_row_bytes(128, _lib.MJ_KV_E2M3) == 96
     assert lib.mj_row_bytes(128, _lib.MJ_KV_FP8_E4M3) == 128
     assert lib.mj_row_bytes(130, _lib.MJ_KV_E2M3) == -1

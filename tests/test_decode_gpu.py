@@ -283,3 +283,34 @@ def test_tc_zero_length_padding_request():
     got = out[: c.b].view(c.b, c.h_q, c.d)
     assert (got[1] == 0).all()
     assert_close_fp32(got, ref, what="padding request")
+
+
+@pytest.mark.parametrize("kv_format,q_len,h_q", [("e2m3", 1, 32), ("fp8", 1, 16), ("e2m3", 6, 64)])
+def test_wait_limit_runs_out_and_the_next_call_is_exact(kv_format, q_len, h_q):
+    """A pipeline wait that runs out: with a 1 ns limit no TMA copy lands in
+    time, so the first wait on one gives up. The launch still ends by itself
+    (every role stops at its next wait, lets its copies and MMAs in flight
+    finish and frees its tensor memory), the status word reads
+    MJ_DEV_TIMEOUT, and the same call with the default limit right after is
+    exact. One-warpgroup (e2m3 with a converter warpgroup, fp8) and
+    three-warpgroup (48 rows per KV head) variants."""
+    from mjolnir_b200 import _lib
+    from mjolnir_b200.runner import _stream
+
+    c = Case(seq_lens=(3000, 1200, 700), q_len=q_len, h_q=h_q, h_k=8, kv_format=kv_format, seed=31, layout="BHN2D")
+    r = c.runner(kernel="tc")
+    plan = r.plan(c.seq_lens, c.b, q_len, c.block_table, c.seq_lens_t)
+    T = c.b * q_len
+    out = torch.zeros(T, c.h_q * c.d, device="cuda")
+    args = r.decode_args(plan, c.query, out, c.k_view, c.v_view, c.dev(c.kd), c.dev(c.vd), 1.0 / math.sqrt(c.d),
+                         q_mul=c.dev(c.q_mul), o_mul=c.dev(c.o_mul))
+    assert _lib.KERNEL_NAMES[_lib.decode_kernel(args)] == "decode_tc"
+    args.wait_limit_ns = 1
+    _lib.decode(args, _stream())
+    torch.cuda.synchronize()
+    with pytest.raises(_lib.MjolnirError, match=f"device status {_lib.MJ_DEV_TIMEOUT}"):
+        r.check_status()
+    assert int(r.status.item()) == 0  # check_status cleared it
+    out, _, _ = c.run(kernel="tc")
+    ref, _ = c.oracle()
+    assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"{kv_format} q_len {q_len} after a timed-out launch")
