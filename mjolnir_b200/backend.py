@@ -118,50 +118,73 @@ def layers_of(vllm_config, layer_names) -> dict:
         return {}
 
 
+# Attention features a layer may switch on that the decode kernel has no code
+# for: the impl attribute, the values that mean "off" and the name reported.
+# Tensor-valued features (sinks, ALiBi slopes) are off only when absent.
+_LAYER_FEATURES = (
+    ("sliding_window", (-1, (-1, -1)), "sliding window"),
+    ("logits_soft_cap", (0, 0.0), "logits soft-cap"),
+    ("sinks", (), "attention sinks"),
+    ("alibi_slopes", (), "ALiBi"),
+)
+
+
+def _feature_on(value, off_values) -> bool:
+    if value is None:
+        return False
+    if isinstance(value, (int, float, tuple)):
+        return value not in off_values
+    return True  # a tensor or a list of per-head values
+
+
 def layer_reason(impl) -> str | None:
-    """Per-layer features the decode kernel does not implement."""
-    sw = getattr(impl, "sliding_window", None)
-    if sw not in (None, (-1, -1), -1):
-        return "sliding window"
-    if getattr(impl, "logits_soft_cap", None) not in (None, 0, 0.0):
-        return "logits soft-cap"
-    if getattr(impl, "sinks", None) is not None:
-        return "attention sinks"
-    if getattr(impl, "alibi_slopes", None) is not None:
-        return "ALiBi"
+    """The first per-layer feature of ``impl`` the decode kernel lacks, or
+    None (the same features as the reference's ``backend.py:263-273``)."""
+    for attr, off_values, name in _LAYER_FEATURES:
+        if _feature_on(getattr(impl, attr, None), off_values):
+            return name
     return None
+
+
+def _config_problems(kv_cache_spec, layer_names, vllm_config):
+    """Every reason the kernel cannot serve this KV-cache group, cheapest
+    checks first (the conditions of the reference's ``backend.py:276-301``)."""
+    if env_flag("MJOLNIR_ATTN_DISABLE").lower() in ("1", "true", "yes"):
+        yield "MJOLNIR_ATTN_DISABLE set"
+    # what the cache holds and how it is paged
+    dtype = str(getattr(vllm_config.cache_config, "cache_dtype", "auto"))
+    if dtype not in MJOLNIR_CACHE_DTYPES:
+        yield f"kv cache dtype {dtype!r} is neither of the kernel's formats {sorted(MJOLNIR_CACHE_DTYPES)}"
+    page = getattr(kv_cache_spec, "block_size", None)
+    if page not in SUPPORTED_PAGE_SIZES:
+        yield f"block size {page} is not a kernel page size {SUPPORTED_PAGE_SIZES}"
+    if getattr(kv_cache_spec, "sliding_window", None):
+        yield "the KV spec keeps a sliding window"
+    # head geometry and model precision
+    d_k = getattr(kv_cache_spec, "head_size", None)
+    if d_k not in (128, 256):
+        yield f"head_size {d_k}: the kernel is built for 128 and 256"
+    d_v = getattr(kv_cache_spec, "head_size_v", None) or d_k
+    if d_v != d_k:
+        yield f"K/V head sizes differ ({d_k} vs {d_v})"
+    model_dtype = vllm_config.model_config.dtype
+    if model_dtype not in (torch.bfloat16, torch.float16):
+        yield f"model dtype {model_dtype} (bf16 or fp16 activations only)"
+    # sequences split across ranks need a cross-rank softmax the kernel lacks
+    pc = vllm_config.parallel_config
+    for kind in ("decode", "prefill"):
+        if getattr(pc, f"{kind}_context_parallel_size", 1) > 1:
+            yield f"{kind} context parallel"
+    # per-layer attention features
+    for name, layer in layers_of(vllm_config, layer_names).items():
+        why = layer_reason(getattr(layer, "impl", None))
+        if why:
+            yield f"layer {name}: {why}"
 
 
 def ineligible_reason(kv_cache_spec, layer_names, vllm_config) -> str | None:
-    """Why this KV-cache group cannot run on the kernel, or None
-    (reference ``backend.py:270-300``)."""
-    if env_flag("MJOLNIR_ATTN_DISABLE").lower() in ("1", "true", "yes"):
-        return "MJOLNIR_ATTN_DISABLE set"
-    cache_dtype = str(getattr(vllm_config.cache_config, "cache_dtype", "auto"))
-    if cache_dtype not in MJOLNIR_CACHE_DTYPES:
-        return f"kv cache dtype {cache_dtype!r} (the kernel reads fp8_e4m3 or fp6_e2m3)"
-    head = getattr(kv_cache_spec, "head_size", None)
-    if head not in (128, 256):
-        return f"head_size {head} (the kernel runs 128 or 256)"
-    if (getattr(kv_cache_spec, "head_size_v", None) or head) != head:
-        return "K/V head sizes differ"
-    if getattr(kv_cache_spec, "sliding_window", None):
-        return "sliding-window KV spec"
-    bs = getattr(kv_cache_spec, "block_size", None)
-    if bs not in SUPPORTED_PAGE_SIZES:
-        return f"block size {bs} (supported: {SUPPORTED_PAGE_SIZES})"
-    if vllm_config.model_config.dtype not in (torch.bfloat16, torch.float16):
-        return f"model dtype {vllm_config.model_config.dtype}"
-    pc = vllm_config.parallel_config
-    if getattr(pc, "decode_context_parallel_size", 1) > 1:
-        return "decode context parallel"
-    if getattr(pc, "prefill_context_parallel_size", 1) > 1:
-        return "prefill context parallel"
-    for name, layer in layers_of(vllm_config, layer_names).items():
-        r = layer_reason(getattr(layer, "impl", None))
-        if r:
-            return f"layer {name}: {r}"
-    return None
+    """The first reason this KV-cache group cannot run on the kernel, or None."""
+    return next(_config_problems(kv_cache_spec, layer_names, vllm_config), None)
 
 
 # ---------------------------------------------------------------------------
@@ -194,17 +217,23 @@ def check_fp6(kernel_reason: str | None, layer_names) -> None:
 
 
 def set_layer_scale(layer, name: str, value: torch.Tensor) -> None:
-    """Replace a layer's k/v scale keeping its kind (Parameter, buffer or
-    attribute) and the float mirror vLLM keeps beside it."""
-    cur = getattr(layer, name, None)
-    if isinstance(cur, torch.nn.Parameter):
-        setattr(layer, name, torch.nn.Parameter(value, requires_grad=False))
-    elif name in getattr(layer, "_buffers", {}):
+    """Point a layer's ``_k_scale`` / ``_v_scale`` at ``value``.
+
+    The attribute is rebound the way the layer registered it -- checkpoints
+    with quantized KV register it as a Parameter, others as a buffer or a
+    plain tensor -- so that ``nn.Module.__setattr__`` accepts the new value
+    and state-dict consumers still find it; vLLM's float copy
+    (``_k_scale_float``) follows when the scale is a single number."""
+    registered = getattr(layer, name, None)
+    if isinstance(registered, torch.nn.Parameter):
+        value = torch.nn.Parameter(value, requires_grad=False)
+    if name in getattr(layer, "_buffers", {}):
         layer._buffers[name] = value
     else:
         setattr(layer, name, value)
-    if value.numel() == 1 and hasattr(layer, name + "_float"):
-        setattr(layer, name + "_float", float(value.reshape(-1)[0].item()))
+    mirror = name + "_float"
+    if value.numel() == 1 and hasattr(layer, mirror):
+        setattr(layer, mirror, float(value.detach().reshape(-1)[0]))
 
 
 def fp6_layer_state(ks, vs, h_r: int, device, fallback: str) -> dict[str, torch.Tensor]:
@@ -246,13 +275,14 @@ def install_fp6_scales(vllm_config, layer_names, h_k: int, d: int) -> int:
     path = kvscales.scales_path()
     if not path:
         raise ValueError(
-            "kv cache dtype fp6_e2m3 needs calibrated scales: set MJOLNIR_ATTN_KV_SCALES to a "
-            "mjolnir.kv_scales file (a calibration run on fp8 KV with MJOLNIR_ATTN_KV_CALIBRATE=1)"
+            "an fp6_e2m3 cache is written with calibrated scales, and MJOLNIR_ATTN_KV_SCALES names no "
+            "scales file; serve the model once on fp8 KV with MJOLNIR_ATTN_KV_CALIBRATE=1 to write one"
         )
     doc = kvscales.load(path)
     missing = kvscales.missing_layers(doc, layer_names)
     if missing:
-        raise ValueError(f"{path} has no scales for {missing[:3]}{' ...' if len(missing) > 3 else ''}")
+        shown = ", ".join(missing[:3]) + (", ..." if len(missing) > 3 else "")
+        raise ValueError(f"scales file {path} lacks {len(missing)} attention layer(s) of this model: {shown}")
     layers = layers_of(vllm_config, layer_names)
     for name, layer in layers.items():
         ks, vs = kvscales.e2m3_scales(doc, name, h_k, d)

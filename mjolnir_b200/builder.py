@@ -185,22 +185,24 @@ class MjolnirMetadataBuilder(_BaseBuilder):  # type: ignore[misc, valid-type]
 
     # -- build -------------------------------------------------------------------
     def kernel_step_q_len(self, cam) -> int | None:
-        """The step's q_len when the kernel can take it, else None
-        (reference ``builder.py:309-343``)."""
-        runner = self.runner
-        if runner is None:
-            return None
+        """The q_len of a step the kernel can run, else None.
+
+        A kernel step is a uniform batch -- every request brings q_len query
+        tokens (one decode token, or the verified token plus the drafts), with
+        CUDA-graph padding requests bringing none -- that fits the runner, under
+        a causal mask or, when enabled, a parallel drafter's non-causal block,
+        and without decode context parallelism (the step routing of the
+        reference's ``builder.py:309-343``)."""
+        r = self.runner
         q_len = int(cam.max_query_len)
-        if not 1 <= q_len <= runner.max_q_len or cam.num_reqs > runner.max_num_seqs:
+        mask = getattr(cam, "causal", True)
+        fits = (r is not None and 1 <= q_len <= r.max_q_len and cam.num_reqs <= r.max_num_seqs
+                and (mask is True or (mask is False and _NONCAUSAL))
+                and getattr(cam, "dcp_local_seq_lens", None) is None)
+        if not fits:
             return None
-        causal = getattr(cam, "causal", True)
-        if causal is not True and not (causal is False and _NONCAUSAL):
-            return None
-        if getattr(cam, "dcp_local_seq_lens", None) is not None:
-            return None
-        if q_len == 1 and cam.num_actual_tokens <= cam.num_reqs:
-            return 1
-        return q_len if uniform_q_len(cam.query_start_loc_cpu, cam.num_reqs, q_len) else None
+        one_token_each = q_len == 1 and cam.num_actual_tokens <= cam.num_reqs
+        return q_len if one_token_each or uniform_q_len(cam.query_start_loc_cpu, cam.num_reqs, q_len) else None
 
     @staticmethod
     def seq_lens_host(cam):

@@ -1,31 +1,40 @@
 """Host-side split-KV planning for the decode kernel.
 
-The unit of work is a contiguous chunk of 128-row KV tiles of one sequence,
-(seq, tile_begin, tile_end, split); the decode grid runs one CTA per (work
-item, KV head), and sequences cut into several chunks are merged by the LSE
-combine.
+A work item is a contiguous run of 128-row KV tiles of one sequence,
+``(seq, tile_begin, tile_end, split)``. The decode runs one job per (work
+item, KV head [, row group]) on persistent CTAs that stride through the job
+list, and a sequence cut into several items has its partial outputs merged by
+the LSE combine.
 
-``plan_split_kv`` keeps the reference's occupancy-pinned rule
-(GoBrrr-ai/mjolnir ``src/mjolnir/mjolnir/arch/thor/plan.py:140-197``, the
-FlashDecoding / FlashInfer scheme): one wave holds
-``slots = sm_count * ctas_per_sm // (heads_k * n_q_tiles)`` work items; when
-the batch is smaller than a wave, the SMALLEST chunk whose total work fits one
-wave is chosen; items are ordered longest first and optionally padded to a
-fixed length with empty items so a CUDA graph replays a fixed grid.
+Every plan is fixed by one number, the chunk length in tiles: sequence ``b``
+with ``t_b`` tiles becomes ``ceil(t_b / chunk)`` items of ``chunk`` tiles (the
+last one shorter), listed longest first (ties keep sequence order) and
+optionally padded with empty items to a fixed length for CUDA-graph replay.
 
-B200 addition (``rebalance=True``): when the batch alone fills a wave the
-reference does not split at all, which on 148 SMs leaves a ragged last wave
-(e.g. 64 sequences x 8 KV heads = 512 CTAs = 1.73 waves of 296). The planner
-then evaluates every chunk size ceil(T / k), k = 1 .. max_splits, with a
-longest-first wave model -- the sum over waves of the longest item in each
-wave, plus a per-item overhead -- and keeps the cheapest. The overhead
-(2 tiles) is the tensor-core kernel's measured per-job cost: preparing the
-job's Q and writing its O / partials take about as long as two 128-row tiles.
-``rebalance=False`` reproduces the reference plan exactly.
+How the chunk is chosen:
+
+* the contract of the reference (GoBrrr-ai/mjolnir
+  ``src/mjolnir/mjolnir/arch/thor/plan.py:140-197``), kept exactly with
+  ``rebalance=False``: a wave holds ``slots = sm_count * ctas_per_sm //
+  (heads_k * n_q_tiles)`` items; a batch of at least one wave is not split,
+  a smaller one gets the shortest chunk whose items still fit in one wave;
+  ``max_splits`` bounds the items per sequence from below on the chunk.
+* the B200 rebalance (``rebalance=True``, the default) scores the
+  reference's chunk and every ``ceil(T / k)``, k = 1 .. max_splits, with a
+  persistent-grid model: CTA ``j`` runs items ``j, j + slots, ...`` of the
+  sorted list, so the step takes the sum over rounds of each round's longest
+  item, plus a per-item cost (``item_overhead`` tiles: preparing a job's Q and
+  writing its output cost about two tiles on the tensor-core kernel) and a
+  quarter tile for the combine launch when anything splits. The cheapest
+  chunk wins; on a tie the longer one. This fixes both ragged last rounds of
+  large batches (64 sequences x 8 KV heads = 512 jobs on 296 slots) and
+  batches a little smaller than a wave, which the reference leaves unsplit
+  (256 sequences x 1 KV head on 296 slots idles 40 slots for the whole step).
 """
 
 from __future__ import annotations
 
+import bisect
 import math
 
 import numpy as np
@@ -34,11 +43,13 @@ TILE_ROWS = 128  # KV rows per tile (the kernel's unit)
 
 
 class SplitPlan:
+    """The work list of one decode step and what was decided to build it."""
+
     def __init__(self, work, n_splits, chunk_tiles, slots):
-        self.work = work  # list of (seq, tile_begin, tile_end, split)
-        self.n_splits = n_splits  # chunks per sequence
+        self.work = work  # [(seq, tile_begin, tile_end, split)], longest first, then padding
+        self.n_splits = n_splits  # items per sequence
         self.chunk_tiles = chunk_tiles
-        self.slots = slots
+        self.slots = slots  # items one round of the persistent grid runs at once
 
     @property
     def num_work(self) -> int:
@@ -46,29 +57,57 @@ class SplitPlan:
 
     @property
     def max_splits_used(self) -> int:
-        return max(self.n_splits) if self.n_splits else 1
+        return max(self.n_splits, default=1)
 
     def work_array(self) -> np.ndarray:
-        w = np.asarray(self.work if self.work else [(0, 0, 0, 0)], dtype=np.int32)
-        return w.reshape(-1, 4)
+        rows = self.work or [(0, 0, 0, 0)]
+        return np.asarray(rows, dtype=np.int32).reshape(-1, 4)
 
     def __repr__(self):
-        real = sum(1 for w in self.work if w[2] > w[1])
-        pad = self.num_work - real
-        return (
-            f"SplitPlan(chunk={self.chunk_tiles} tiles, work={real}{f'+{pad} pad' if pad else ''}, "
-            f"slots/wave={self.slots}, max chunks/seq={self.max_splits_used})"
-        )
+        used = [w for w in self.work if w[2] > w[1]]
+        extra = self.num_work - len(used)
+        pad = f" (+{extra} empty)" if extra else ""
+        return (f"<SplitPlan {len(used)} items{pad} of <= {self.chunk_tiles} tiles, {self.slots} per round, "
+                f"<= {self.max_splits_used} per sequence>")
 
 
-def _wave_cost(tiles: np.ndarray, chunk: int, slots: int, item_overhead: float) -> float:
-    """Longest-first wave model of the decode time, in tile units."""
-    k = np.ceil(tiles / chunk).astype(np.int64)
-    full = np.repeat(np.full(len(tiles), chunk, dtype=np.int64), np.maximum(k - 1, 0))
-    last = tiles - (k - 1) * chunk
-    lens = np.sort(np.concatenate([full, last]))[::-1]
-    wave_heads = lens[::slots]  # longest item of each wave
-    return float(wave_heads.sum() + item_overhead * len(wave_heads)) + (0.25 if k.max() > 1 else 0.0)
+def _items_for(tiles, chunk: int) -> int:
+    return sum(-(-t // chunk) for t in tiles)
+
+
+def _reference_chunk(tiles, slots: int, shortest: int) -> int:
+    """The reference's choice: no split once the batch fills a round, else the
+    shortest chunk (not below `shortest`) whose items fit in one round."""
+    longest = max(tiles)
+    if len(tiles) >= slots or shortest >= longest:
+        return longest
+    candidates = range(shortest, longest + 1)  # item count falls as the chunk grows
+    return candidates[bisect.bisect_left(candidates, True, key=lambda c: _items_for(tiles, c) <= slots)]
+
+
+def _round_cost(tiles: np.ndarray, chunk: int, slots: int, item_overhead: float) -> float:
+    """Model of a persistent-grid step, in tiles: sum over rounds of each
+    round's longest item plus `item_overhead` per round, plus 0.25 for the
+    combine launch when some sequence splits."""
+    per_seq = -(-tiles // chunk)
+    lengths = np.full(int(per_seq.sum()), chunk, dtype=np.int64)
+    ends = np.cumsum(per_seq) - 1  # each sequence's last (possibly shorter) item
+    lengths[ends] = tiles - (per_seq - 1) * chunk
+    lengths[::-1].sort()  # longest first
+    leaders = lengths[::slots]  # round r starts with item r * slots, the longest of its round
+    return float(leaders.sum()) + item_overhead * len(leaders) + (0.25 if per_seq.max() > 1 else 0.0)
+
+
+def _cheapest_chunk(tiles, slots: int, shortest: int, max_splits: int, ref_chunk: int, item_overhead: float) -> int:
+    longest = max(tiles)
+    options = {max(shortest, -(-longest // k)) for k in range(1, max_splits + 1)} | {ref_chunk}
+    t = np.asarray(tiles, dtype=np.int64)
+    best_chunk, best_cost = None, math.inf
+    for chunk in sorted(options, reverse=True):  # a longer chunk keeps a tie
+        cost = _round_cost(t, chunk, slots, item_overhead)
+        if cost < best_cost - 1e-9:
+            best_chunk, best_cost = chunk, cost
+    return best_chunk
 
 
 def plan_split_kv(
@@ -84,43 +123,25 @@ def plan_split_kv(
     rebalance: bool = True,
     item_overhead: float = 2.0,
 ) -> SplitPlan:
-    tiles = [max(1, math.ceil(int(L) / TILE_ROWS)) for L in seq_lens]
-    T = max(tiles)
+    tiles = [max(1, -(-int(L) // TILE_ROWS)) for L in seq_lens]
+    longest = max(tiles)
     slots = max(1, (sm_count * ctas_per_sm) // (heads_k * n_q_tiles))
-    lo = max(min_chunk_tiles, math.ceil(T / max_splits))  # cap chunks per sequence
+    shortest = max(min_chunk_tiles, -(-longest // max_splits))  # at most max_splits items per sequence
     if force_splits > 0:
-        chunk = max(lo, math.ceil(T / force_splits))
+        chunk = max(shortest, -(-longest // force_splits))
     elif max_splits == 1:
-        chunk = T
-    elif len(tiles) >= slots:
-        chunk = T
-        if rebalance:
-            t = np.asarray(tiles, dtype=np.int64)
-            cands = sorted({max(lo, math.ceil(T / k)) for k in range(1, max_splits + 1)}, reverse=True)
-            best = None
-            for c in cands:
-                cost = _wave_cost(t, c, slots, item_overhead)
-                if best is None or cost < best[0] - 1e-9:
-                    best = (cost, c)
-            chunk = best[1]
+        chunk = longest
     else:
-        hi = T
-        while lo < hi:  # smallest chunk whose total work fits one wave
-            mid = (lo + hi) // 2
-            if sum(math.ceil(t / mid) for t in tiles) <= slots:
-                hi = mid
-            else:
-                lo = mid + 1
-        chunk = lo
-    work, n_splits = [], []
-    for b, t in enumerate(tiles):
-        k = math.ceil(t / chunk)
-        n_splits.append(k)
-        work.extend((b, j * chunk, min((j + 1) * chunk, t), j) for j in range(k))
-    work.sort(key=lambda w: -(w[2] - w[1]))  # longest first (stable)
+        chunk = _reference_chunk(tiles, slots, shortest)
+        if rebalance:
+            chunk = _cheapest_chunk(tiles, slots, shortest, max_splits, chunk, item_overhead)
+    n_splits = [-(-t // chunk) for t in tiles]
+    items = [(b, s * chunk, min(t, (s + 1) * chunk), s) for b, t in enumerate(tiles) for s in range(n_splits[b])]
+    items.sort(key=lambda w: w[1] - w[2])  # longest first; sort is stable
     if pad_to:
-        if pad_to < len(work):
-            raise ValueError(f"pad_to {pad_to} < {len(work)} work items")
-        work += [(0, 0, 0, 0)] * (pad_to - len(work))
-    assert max(n_splits) <= max_splits
-    return SplitPlan(work, n_splits, chunk, slots)
+        if pad_to < len(items):
+            raise ValueError(f"pad_to {pad_to} is below the {len(items)} work items of this plan")
+        items.extend([(0, 0, 0, 0)] * (pad_to - len(items)))
+    if max(n_splits) > max_splits:
+        raise AssertionError(f"plan cut a sequence into {max(n_splits)} > max_splits {max_splits} items")
+    return SplitPlan(items, n_splits, chunk, slots)

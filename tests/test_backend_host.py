@@ -96,7 +96,7 @@ def test_register_points_custom_at_the_backend(monkeypatch):
         def __class_getitem__(cls, k):
             return k
 
-    monkeypatch.setattr(mjolnir_b200, "_registry", lambda: (Enum, lambda member, path: calls.append((member, path))))
+    monkeypatch.setattr(mjolnir_b200, "_backend_registry", lambda: (Enum, lambda member, path: calls.append((member, path))))
     mjolnir_b200.register()
     assert calls == [("CUSTOM", "mjolnir_b200.backend.MjolnirAttentionBackend")]
     monkeypatch.setenv("MJOLNIR_ATTN_DISABLE", "1")
