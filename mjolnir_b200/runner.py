@@ -466,10 +466,15 @@ class DecodeRunner:
         return _lib.KERNEL_NAMES[_lib.decode_kernel(args)]
 
     def check_status(self) -> None:
-        """Raise if a kernel flagged a bad page / split index (synchronizes)."""
+        """Raise if a kernel flagged a bad page / split index or a wait that
+        ran out (synchronizes). The status word is cleared, and so are the
+        in-kernel merge counters: a job that stopped early never counted
+        itself in, and a stale count would let the next launch merge before
+        every split had written its partials."""
         code = int(self.status.item())
         if code != _lib.MJ_DEV_OK:
             self.status.zero_()
+            self.merge_counters.zero_()
             raise _lib.MjolnirError(_lib.MJ_ERR_DEVICE, f"device status {code}")
 
 

@@ -63,6 +63,22 @@ def test_noalloc_matches_decode_two_calls_in_a_row():
     assert_close_fp32(got2, oracle2, what="noalloc call 2 vs oracle")
 
 
+def test_noalloc_with_in_kernel_merge():
+    """With merge counters (a runner built with fused_merge) the tensor-core
+    kernel merges the splits itself, reading the partials back from the
+    built-in array: the result still equals mj_decode's, on two calls."""
+    c = Case(seq_lens=(6000, 2500, 700), h_q=32, h_k=8, kv_format="e2m3", seed=24, outliers=0.01)
+    r = c.runner(fused_merge=True)
+    plan = r.plan(c.seq_lens, c.b, 1, c.block_table, c.seq_lens_t)
+    assert plan.with_reduction and int(plan.n_splits.max()) <= 16  # the in-kernel merge takes <= 16 splits
+    for call in (1, 2):
+        ref, got = _decode_both(c, r, plan)
+        assert_close_fp32(got, ref, what=f"noalloc with the in-kernel merge, call {call}")
+    oracle, _ = c.oracle()
+    assert_close_fp32(got, oracle, what="noalloc with the in-kernel merge vs oracle")
+    assert int(r.merge_counters.abs().sum()) == 0  # the last job of each split group reset its counter
+
+
 def test_noalloc_refuses_oversized_partials():
     from mjolnir_b200 import _lib
 
