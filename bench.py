@@ -53,11 +53,32 @@ WORKLOADS = {
 
 
 def seq_lens_for(w, seed=1234):
+    """Context lengths of a workload. cfg3: log-normal with median 8192 and
+    sigma 0.75 (the config fixes the median and the clip range, not sigma),
+    drawn in float32 from torch's CPU generator seeded 1234 and clipped to
+    [512, 32768]: sum 1,317,124 tokens."""
     if w["L"] == "lognormal":
-        rng = np.random.default_rng(seed)
-        L = np.round(np.exp(np.log(8192.0) + 0.75 * rng.standard_normal(w["b"])))
-        return np.clip(L, 512, 32768).astype(np.int64).tolist()
+        g = torch.Generator().manual_seed(seed)
+        z = torch.randn(w["b"], generator=g)
+        L = torch.exp(math.log(8192.0) + 0.75 * z).round().clamp(512, 32768)
+        return [int(x) for x in L.tolist()]
     return [int(w["L"])] * w["b"]
+
+
+def workload_config(name, kv, world, page_size=None, batch=None, seed=1234):
+    """The `config` object of a bench line: the workload only (shapes, format,
+    lengths, sharding), the same for our arm and the reference arm."""
+    w = dict(WORKLOADS[name])
+    kv = kv or w["kv"]
+    if page_size:
+        w["PS"] = page_size
+    if batch:
+        w["b"] = batch
+    lens = seq_lens_for(w, seed)
+    return {"workload": name, "kv_format": kv, "batch": w["b"], "h_q": w["h_q"], "h_k": w["h_k"],
+            "head_dim": w["d"], "q_len": w["q_len"], "page_size": w["PS"], "sum_seq_len": int(sum(lens)),
+            "parallelism": f"tp{world} (KV heads)", "l2": "KV stream per step > 126 MB L2 (no flush needed)",
+            "kv_bytes_per_step": kv_bytes(lens, w["h_k"], w["d"], kv)}
 
 
 VMAX = {"e2m3": 7.5, "e3m2": 28.0, "e2m1": 6.0}  # largest code value of each narrow format
@@ -348,12 +369,13 @@ def run_reference_arm(args, rank, world):
         times.append(dt)
     mean = sum(times) / len(times)
     gbs = nbytes / mean / 1e9
-    sample = f"1 sequence of {name} (all {WORKLOADS[name]['h_k']} KV heads, L={seq_lens_for(WORKLOADS[name])[0]}) per step"
+    sample = (f"per step 1 sequence of {name} (all {WORKLOADS[name]['h_k']} KV heads, "
+              f"L={seq_lens_for(WORKLOADS[name])[0]}, {nbytes} KV bytes): dequantise + fp32 attend")
     line = {
         "impl": "reference", "metric": "decode-attn KV GB/s", "value": round(gbs, 4), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic", "config": {"workload": name, "kv_format": kv},
+        "data": "synthetic", "config": workload_config(name, kv, world, args.page_size, args.batch),
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -517,12 +539,8 @@ def main():
         "vs_baseline": None,
         "dtype": "fp8-e4m3 KV" if wl.fmt == "fp8" else f"{wl.fmt} KV",
         "data": "synthetic (N(0,1) K/V quantized by the repo's write kernel, shuffled pages, random Q)",
-        "config": {"workload": args.workload, "kv_format": wl.fmt, "batch": wl.b, "h_q": WORKLOADS[args.workload]["h_q"],
-                   "h_k": WORKLOADS[args.workload]["h_k"], "head_dim": wl.d, "q_len": wl.q_len,
-                   "page_size": wl.PS, "sum_seq_len": int(sum(wl.lens)), "parallelism": f"tp{world} (KV heads)",
-                   "l2": "KV stream per step > 126 MB L2 (no flush needed)",
-                   "kv_bytes_per_step": total_kv, "chunk_tiles": wl.plan.chunk_tiles,
-                   "work_items": wl.plan.num_chunks},
+        "config": workload_config(args.workload, wl.fmt, world, args.page_size, args.batch),
+        "plan": {"chunk_tiles": wl.plan.chunk_tiles, "work_items": wl.plan.num_chunks, "kernel": kname},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": kname, "peak_source": peak_kind,

@@ -199,13 +199,15 @@ typedef struct mj_decode_args {
   const void* v_scales;
   int64_t ks_stride_page, ks_stride_row, ks_stride_head; /* bytes */
   int64_t vs_stride_page, vs_stride_row, vs_stride_head; /* bytes */
-  /* Limit of each wait inside the tensor-core kernel's pipeline, in ns; 0 =
-   * the built-in 0.5 s (a tile takes microseconds). A wait that runs out
-   * sets MJ_DEV_TIMEOUT in the status word; the kernel then stops, lets its
-   * copies and MMAs in flight finish, frees its tensor memory and returns,
-   * leaving the context usable (the reference's pipeline waits are
-   * unbounded). Tests shorten it to make a wait run out on purpose. */
-  uint64_t wait_limit_ns;
+  /* Test hook for the kernel's abort path; 0 in normal use. Every wait
+   * inside the tensor-core kernel's pipeline is bounded (0.5 s; a tile takes
+   * microseconds) and a wait that runs out sets MJ_DEV_TIMEOUT in the status
+   * word; the kernel then stops, lets its copies and MMAs in flight finish,
+   * frees its tensor memory and returns, leaving the context usable (the
+   * reference's pipeline waits are unbounded). When non-zero, the MMA issuer
+   * of every CTA first waits this many ns on a phase that nothing completes,
+   * so that path runs on a normal launch. */
+  uint64_t abort_probe_ns;
 } mj_decode_args;
 
 int mj_decode(const mj_decode_args* args, void* stream);

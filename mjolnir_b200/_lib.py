@@ -120,7 +120,7 @@ class DecodeArgs(C.Structure):
         ("k_scales", _vp), ("v_scales", _vp),
         ("ks_stride_page", _i64), ("ks_stride_row", _i64), ("ks_stride_head", _i64),
         ("vs_stride_page", _i64), ("vs_stride_row", _i64), ("vs_stride_head", _i64),
-        ("wait_limit_ns", C.c_uint64),
+        ("abort_probe_ns", C.c_uint64),
     ]
 
 

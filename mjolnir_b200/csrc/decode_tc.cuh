@@ -31,14 +31,17 @@
 //   e4m3 scale per 16) converts K and V: each slot becomes
 //   e4m3(code * scale * 2^-3), its scale rows arriving with the stage.
 //
-// Numerics: split-fp8 Q and P carry ~12 significant bits each
-// (hi + mid / 16 + lo / 256), accumulation is fp32 in TMEM, softmax is fp32;
+// Numerics: split-fp8 Q carries ~12 significant bits (hi + mid / 16 + lo /
+// 256 of the fp32 value), P the 11 of its f16 rounding (the same three terms
+// hold it exactly); accumulation is fp32 in TMEM, the softmax is fp32;
 // the reference's single-e4m3 recipe (arch/thor/decode.py:1288-1297) is not
 // used because it misses the 2e-3 tolerance.
 //
-// Every mbarrier wait is bounded (wait_ns); on a timeout the CTA sets
+// Every mbarrier wait is bounded (MJ_TC_WAIT_NS); on a timeout the CTA sets
 // MJ_DEV_TIMEOUT in the status word, all roles stop at their next wait, wait
 // (bounded) for their in-flight copies and MMAs, free TMEM and return.
+// mj_decode_args.abort_probe_ns makes the S issuer start with a wait that
+// runs out, to exercise that path.
 #pragma once
 
 #include <limits.h>
@@ -50,6 +53,9 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#ifndef MJ_CVT_BALANCED
+#define MJ_CVT_BALANCED 1
+#endif
 #ifndef MJ_TC_WAIT_NS
 #define MJ_TC_WAIT_NS 500000000ull  // 0.5 s per wait: a tile takes microseconds
 #endif
@@ -62,11 +68,14 @@ using namespace sm100;
 constexpr int kTileBytes = 128 * 128;  // one 128 x 128 byte operand tile (e2m3: 16U6 slots)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-// The running max is raised only when a score exceeds it by more than
-// 2^kRescaleLog2 (the rest of the time no cross-thread max is needed), so
-// p <= 2^kRescaleLog2 and p * kPScale <= 448 fits e4m3.
+// The running max m is raised only when a score exceeds it by more than
+// kRescaleLog2 (log2 units; the rest of the time no cross-thread max is
+// needed), so p = 2^(s - m) <= 2^8. The softmax keeps m' = m - log2(448/256)
+// instead of m, so 2^(s - m') = p * 448/256 <= 448 fits e4m3 as written, the
+// row sums carry the same factor (it cancels in O = sum(p' v) / sum(p')), and
+// the LSE is m' + log2(sum p') unchanged.
 constexpr float kRescaleLog2 = 8.0f;
-constexpr float kPScale = 448.0f / 256.0f;
+constexpr float kLog2PScale = 0.80735492205760410f;  // log2(448 / 256)
 // the in-kernel split merge holds one partial per split in registers
 constexpr int kMergeMaxSplits = 16;
 
@@ -165,7 +174,11 @@ struct Cfg {
   static constexpr int SM0 = 4 * (1 + CVTW);             // first softmax warp
   static constexpr int THREADS = 128 * (1 + CVTW + NWG);
   static constexpr int CTAS_PER_SM = NWG == 1 ? 2 : 1;
-  static constexpr int CVT_ROLE = 32 + 128 * CVTW;       // threads of the converter role
+  // threads of the converter role: warp 2, or (MJ_CVT_BALANCED) with a
+  // converter warpgroup that warpgroup alone, one converter warp per SM
+  // sub-partition beside each softmax warp
+  static constexpr int CVT_ROLE = (MJ_CVT_BALANCED && CVTW) ? 128 : 32 + 128 * CVTW;
+  static constexpr int CVT_BASE = (MJ_CVT_BALANCED && CVTW) ? 0 : 32;  // converter index of the warpgroup's thread 0
   static constexpr bool SM_CONVERTS = Fmt<FMT>::NARROW && CVTW == 0;  // softmax warpgroups share the conversion
   static constexpr int CVT_THREADS = CVT_ROLE + (SM_CONVERTS ? 128 * NWG : 0);  // threads that convert a V tile
   // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
@@ -196,7 +209,7 @@ struct Cfg {
   static constexpr int Q_OFF = V_OFF + STAGES * kTileBytes;  // two slots (jobs)
   static constexpr int P_OFF = (Q_OFF + 2 * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
   static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;
-  static constexpr int NBARS = 5 * STAGES + 2 * 8 + 1;  // k/v full/empty rings, k_ready ring, 8 pairs, drain
+  static constexpr int NBARS = 5 * STAGES + 2 * 8 + 2;  // k/v full/empty rings, k_ready ring, 8 pairs, drain, never
   static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[NWG][2][4][NQP]
   static constexpr int MISC_OFF = RED_OFF + NWG * 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [NWG][4][NQP]
   // nvfp4: per stage the K then V scale rows of the tile ([128 rows][8 B] each)
@@ -213,6 +226,7 @@ struct Bars {
   uint64_t *s_full, *s_free, *p_full, *o_full, *v_ready, *v_free, *q_full;  // pairs (o_full: PV of tile t done)
   uint64_t* o_free;                                         // once per job: O read out, next job may overwrite
   uint64_t* drain;
+  uint64_t* never;  // nothing arrives on it: the abort-path probe waits on it
 };
 
 
@@ -255,15 +269,21 @@ __device__ __forceinline__ float2 combine3x2(const float* v, int r) {
   return ffma2(lo, make_float2(0.00390625f, 0.00390625f), ffma2(mid, make_float2(0.0625f, 0.0625f), hi));
 }
 
-// split3 on a pair with packed residual arithmetic (the residuals are exact)
-__device__ __forceinline__ void split3x2(float2 y, uint16_t& hb, uint16_t& mb, uint16_t& lb) {
-  const float2 m16 = make_float2(-16.f, -16.f), p16 = make_float2(16.f, 16.f);
-  hb = f2_to_e4m3x2(y.x, y.y);
-  const float2 r1 = ffma2(e4m3x2_to_f2(hb), m16, fmul2(y, p16));
-  mb = f2_to_e4m3x2(r1.x, r1.y);
-  const float2 r2 = ffma2(e4m3x2_to_f2(mb), m16, fmul2(r1, p16));
-  lb = f2_to_e4m3x2(r2.x, r2.y);
+// y0, y1 (0 <= y <= 448) rounded once to f16 and split into three e4m3
+// terms y_h = hi + mid / 16 + lo / 256 in f16 arithmetic: the residuals of an
+// 11-bit value are exact in f16 (Sterbenz) and the three terms hold all of
+// it. Used for P: ten instructions a pair instead of thirteen, at f16
+// precision (relative error <= 2^-12).
+__device__ __forceinline__ void split3x2_h(float2 y, uint16_t& hb, uint16_t& mb, uint16_t& lb) {
+  const __half2 yh = __floats2half2_rn(y.x, y.y);
+  const __half2 k16 = __float2half2_rn(16.f), km16 = __float2half2_rn(-16.f);
+  hb = h2_to_e4m3x2(yh);
+  const __half2 r1 = __hfma2(e4m3x2_to_h2(hb), km16, __hmul2(yh, k16));  // (y - hi) * 16
+  mb = h2_to_e4m3x2(r1);
+  const __half2 r2 = __hfma2(e4m3x2_to_h2(mb), km16, __hmul2(r1, k16));  // (r1 - mid) * 16
+  lb = h2_to_e4m3x2(r2);
 }
+
 
 }  // namespace tc
 }  // namespace mj
@@ -292,7 +312,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   const int h_k = a.h_k;
   // the limit of every pipeline wait (drains keep the default: copies and
   // MMAs in flight must land before the CTA exits, however short this is)
-  const uint64_t wait_ns = a.wait_limit_ns ? a.wait_limit_ns : MJ_TC_WAIT_NS;
+  // every pipeline wait is bounded by MJ_TC_WAIT_NS (a compile-time limit:
+  // a run-time one on every wait measured 1-3 % slower)
+  constexpr uint64_t wait_ns = MJ_TC_WAIT_NS;
   // A job is (work item, KV head, row group): a CTA serves at most RT query
   // rows; a larger GQA x draft group is cut into n_rg row groups whose jobs
   // are adjacent in the list, so CTAs reading the same KV stream run side by
@@ -317,6 +339,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   b.q_full = b.v_free + 2;
   b.drain = b.q_full + 2;
   b.k_ready = b.drain + 1;
+  b.never = b.k_ready + S;
   float* red_all = reinterpret_cast<float*>(sm + C::RED_OFF);   // [NWG][2][4][NQP]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::MISC_OFF + 4);
@@ -346,6 +369,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       mbar_init(&b.q_full[i], NWG);
     }
     mbar_init(b.drain, 2);  // one commit from each MMA issuer
+    mbar_init(b.never, 1);
     *abort_flag = 0;
     never_abort = 0;
     fence_mbar_init();
@@ -611,7 +635,8 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       // ----------------------------------------------------- S = K . Q^T issuer
       if (lane == 0) {
         const uint32_t idesc_s = idesc_f8f6f4(Fmt<FMT>::MMA_FMT, 0u, 0u, 0u, (uint32_t)NS);
-        bool ok = true;
+        // the abort-path probe: a bounded wait on a phase nothing completes
+        bool ok = !a.abort_probe_ns || mbar_wait_rt(b.never, 0, abort_flag, a.abort_probe_ns);
         int it = 0, jc = 0;
         for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
           int seq, tb, te, split, h, g;
@@ -680,12 +705,12 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       }
       __syncwarp();
     } else {
-      convert_role(lane);  // warp 2: converter threads 0..31
+      if (!(MJ_CVT_BALANCED && CVTW)) convert_role(lane);  // warp 2: converter threads 0..31
     }
   } else if (warp < C::SM0) {
     // the converter warpgroup: converter threads 32 .. CVT_ROLE - 1
     if constexpr (C::REG_LO > 0) setmaxnreg_dec<C::REG_LO>();
-    convert_role(32 + (int)threadIdx.x - 128);
+    convert_role(C::CVT_BASE + (int)threadIdx.x - 128);
   } else {
     if constexpr (C::REG_HI > 0) setmaxnreg_inc<C::REG_HI>();
     // -------------------------------------------------- softmax warpgroups
@@ -835,7 +860,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             if (j > lim_of(2 * q + 1)) v.y = -INFINITY;
           }
           x2[q] = v;
-          grow = grow || (v.x > m2[q].x + kRescaleLog2) || (v.y > m2[q].y + kRescaleLog2);
+          grow = grow || (v.x > m2[q].x + (kRescaleLog2 + kLog2PScale)) || (v.y > m2[q].y + (kRescaleLog2 + kLog2PScale));
         }
         // one barrier per tile: a uniform vote on "some score outgrew its row's
         // max" (or abort); only then do the rows exchange their tile maxima
@@ -857,7 +882,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           float cc[NQP];  // correction of each row's earlier sums: 2^(m_old - m_new)
 #pragma unroll
           for (int r = 0; r < NQP; ++r) {
-            const float mt = fmaxf(fmaxf(rd[r], rd[NQP + r]), fmaxf(rd[2 * NQP + r], rd[3 * NQP + r]));
+            const float mt = fmaxf(fmaxf(rd[r], rd[NQP + r]), fmaxf(rd[2 * NQP + r], rd[3 * NQP + r])) - kLog2PScale;
             float& mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
             float& lr = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
             cc[r] = 1.f;
@@ -905,7 +930,6 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         uint32_t w[NW];
 #pragma unroll
         for (int k = 0; k < NW; ++k) w[k] = 0u;
-        const float2 ps2 = make_float2(kPScale, kPScale);
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
           // a row that has seen no key keeps m = -inf and all its scores -inf:
@@ -914,7 +938,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           const float2 pv = make_float2(exp2_approx(d.x), exp2_approx(d.y));
           l2[q] = fadd2(l2[q], pv);
           uint16_t hb, mb, lb;
-          split3x2(fmul2(pv, ps2), hb, mb, lb);
+          split3x2_h(pv, hb, mb, lb);
           const int r = 2 * q, sh = 16 * (q & 1);
           w[r >> 2] |= (uint32_t)hb << sh;
           w[(NQP + r) >> 2] |= (uint32_t)mb << sh;
@@ -984,7 +1008,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         break;
       }
       const bool final_out = nsp <= 1;
-      const float vscale = Fmt<FMT>::V_UNSCALE * vd / kPScale;
+      const float vscale = Fmt<FMT>::V_UNSCALE * vd;
       const int qi0 = row0 / h_r, rr0 = row0 % h_r;
       auto qh_of = [&](int r) { return h * h_r + (rr0 + r) % h_r; };
       auto tok_of = [&](int r) { return (int64_t)seq * q_len + qi0 + (rr0 + r) / h_r; };

@@ -82,9 +82,20 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 
 // Wait for the phase of `parity` to complete, giving up after `limit_ns`
 // (or at once when *abort is already set). Returns false on give-up. The
-// first test does not block, and no suspend outlasts the limit, so a short
-// limit gives up on any phase that is not already complete.
+// first try blocks (the hardware wakes the thread when the phase completes).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
+// As mbar_wait, for a limit known only at run time, possibly short: the first
+// test does not block and no suspend outlasts the limit.
+__device__ __forceinline__ bool mbar_wait_rt(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   const uint32_t hint = limit_ns < 20000u ? (uint32_t)limit_ns : 20000u;
@@ -305,6 +316,19 @@ __device__ __forceinline__ float2 e4m3x2_to_f2(uint16_t v) {
   asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(v));
   __half2 h = *reinterpret_cast<__half2*>(&h2);
   return __half22float2(h);
+}
+
+// Two f16 (a __half2, low half first) -> two e4m3 bytes (round to nearest
+// even, saturating), and back (exact).
+__device__ __forceinline__ uint16_t h2_to_e4m3x2(__half2 v) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(*reinterpret_cast<uint32_t*>(&v)));
+  return r;
+}
+__device__ __forceinline__ __half2 e4m3x2_to_h2(uint16_t v) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(v));
+  return *reinterpret_cast<__half2*>(&h2);
 }
 
 // ---- packed fp32 pairs (Blackwell f32x2 ALU ops) ---------------------------

@@ -53,3 +53,6 @@ def test_our_arm_line():
     assert cb["cores"] >= 1 and cb["value"] > 0 and cb["kind"] in ("port", "reference")
     c = j["clocks"]
     assert "sm_mhz" in c and "sm_max_mhz" in c and "reasons" in c
+    # both arms describe the same workload with the same config object
+    ref = _run("--impl", "reference", "--workload", "cfg2", "--batch", "8", "--steps", "1", "--warmup", "3")
+    assert ref["config"] == j["config"]

@@ -116,12 +116,13 @@ def test_split_and_unsplit_agree(sm_count, kernel):
 
 
 @pytest.mark.parametrize("kv_format", ["fp8", "e2m3"])
-@pytest.mark.parametrize("q_len,h_q", [(1, 8), (2, 8), (1, 32), (3, 16), (6, 16), (8, 16), (5, 16)])
+@pytest.mark.parametrize("q_len,h_q", [(1, 8), (2, 8), (3, 4), (1, 32), (3, 16), (6, 16), (8, 16), (5, 16)])
 def test_tc_rescale_in_later_tiles(kv_format, q_len, h_q):
     """Scores that grow along the sequence make the running max rise after the
     first tile, so O accumulated in TMEM is rescaled in place. Row counts
-    cover the one-warpgroup (4, 8, 16 rows), two- and three-warpgroup (24, 48
-    rows, 40 with padding rows) and row-group (64 rows) variants."""
+    cover the one-warpgroup (4, 8, 16 rows; 6 with padding rows), two- and
+    three-warpgroup (24, 48 rows, 40 with padding rows) and row-group (64
+    rows) variants."""
     c = Case(seq_lens=(2000, 700, 1290), q_len=q_len, h_q=h_q, h_k=2, kv_format=kv_format, layout="BHN2D",
              seed=43 + q_len, k_ramp=2.5)
     out, _, _ = c.run(kernel="tc", sm_count=8)  # few slots: long chunks, many tiles per job
@@ -166,8 +167,8 @@ def test_tc_tensor_parallel_shards(kv_format, h_q, h_k):
 
 @pytest.mark.parametrize("kv_format", ["e3m2", "e2m1"])
 @pytest.mark.parametrize("kernel", ["simt", "tc"])
-@pytest.mark.parametrize("q_len,h_q,page_size,layout", [(1, 8, 16, "BHN2D"), (1, 32, 64, "B2NHD"), (3, 16, 32, "BHN2D"),
-                                                        (6, 16, 16, "B2HND")])
+@pytest.mark.parametrize("q_len,h_q,page_size,layout", [(1, 8, 16, "BHN2D"), (2, 8, 16, "BHN2D"), (1, 16, 32, "B2NHD"),
+                                                        (1, 32, 64, "B2NHD"), (3, 16, 32, "BHN2D"), (6, 16, 16, "B2HND")])
 def test_other_narrow_formats(kv_format, kernel, q_len, h_q, page_size, layout):
     """e3m2 and e2m1 caches (the reference harness's other narrow formats):
     both kernels, one- and several-warpgroup variants, fused and separate
@@ -286,14 +287,14 @@ def test_tc_zero_length_padding_request():
 
 
 @pytest.mark.parametrize("kv_format,q_len,h_q", [("e2m3", 1, 32), ("fp8", 1, 16), ("e2m3", 6, 64)])
-def test_wait_limit_runs_out_and_the_next_call_is_exact(kv_format, q_len, h_q):
-    """A pipeline wait that runs out: with a 1 ns limit no TMA copy lands in
-    time, so the first wait on one gives up. The launch still ends by itself
-    (every role stops at its next wait, lets its copies and MMAs in flight
-    finish and frees its tensor memory), the status word reads
-    MJ_DEV_TIMEOUT, and the same call with the default limit right after is
-    exact. One-warpgroup (e2m3 with a converter warpgroup, fp8) and
-    three-warpgroup (48 rows per KV head) variants."""
+def test_bounded_wait_runs_out_and_the_next_call_is_exact(kv_format, q_len, h_q):
+    """The abort path of the bounded waits: with abort_probe_ns the MMA
+    issuer of every CTA first waits 2 us on a phase nothing completes. The
+    wait gives up, the launch still ends by itself (every role stops at its
+    next wait, lets its copies and MMAs in flight finish and frees its tensor
+    memory), the status word reads MJ_DEV_TIMEOUT, and the same call right
+    after, without the probe, is exact. One-warpgroup (e2m3 with a converter
+    warpgroup, fp8) and three-warpgroup (48 rows per KV head) variants."""
     from mjolnir_b200 import _lib
     from mjolnir_b200.runner import _stream
 
@@ -305,7 +306,7 @@ def test_wait_limit_runs_out_and_the_next_call_is_exact(kv_format, q_len, h_q):
     args = r.decode_args(plan, c.query, out, c.k_view, c.v_view, c.dev(c.kd), c.dev(c.vd), 1.0 / math.sqrt(c.d),
                          q_mul=c.dev(c.q_mul), o_mul=c.dev(c.o_mul))
     assert _lib.KERNEL_NAMES[_lib.decode_kernel(args)] == "decode_tc"
-    args.wait_limit_ns = 1
+    args.abort_probe_ns = 2000
     _lib.decode(args, _stream())
     torch.cuda.synchronize()
     with pytest.raises(_lib.MjolnirError, match=f"device status {_lib.MJ_DEV_TIMEOUT}"):
