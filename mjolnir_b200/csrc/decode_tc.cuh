@@ -31,9 +31,9 @@
 //   e4m3 scale per 16) converts K and V: each slot becomes
 //   e4m3(code * scale * 2^-3), its scale rows arriving with the stage.
 //
-// Numerics: split-fp8 Q carries ~12 significant bits (hi + mid / 16 + lo /
-// 256 of the fp32 value), P the 11 of its f16 rounding (the same three terms
-// hold it exactly); accumulation is fp32 in TMEM, the softmax is fp32;
+// Numerics: split-fp8 Q and P carry ~12 significant bits each (hi + mid /
+// 16 + lo / 256 of the fp32 value), accumulation is fp32 in TMEM, the
+// softmax is fp32;
 // the reference's single-e4m3 recipe (arch/thor/decode.py:1288-1297) is not
 // used because it misses the 2e-3 tolerance.
 //
@@ -210,7 +210,8 @@ struct Cfg {
   static constexpr int P_OFF = (Q_OFF + 2 * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
   static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;
   static constexpr int NBARS = 5 * STAGES + 2 * 8 + 2;  // k/v full/empty rings, k_ready ring, 8 pairs, drain, never
-  static constexpr int RED_OFF = BAR_OFF + NBARS * 8;   // float red[NWG][2][4][NQP]
+  // float red[NWG][2][4][NQP], 16-byte aligned so its rows load as float4
+  static constexpr int RED_OFF = (BAR_OFF + NBARS * 8 + 15) / 16 * 16;
   static constexpr int MISC_OFF = RED_OFF + NWG * 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [NWG][4][NQP]
   // nvfp4: per stage the K then V scale rows of the tile ([128 rows][8 B] each)
   static constexpr int SC_OFF = (MISC_OFF + 64 + NWG * 4 * 4 * NQP + 15) / 16 * 16;
@@ -226,7 +227,6 @@ struct Bars {
   uint64_t *s_full, *s_free, *p_full, *o_full, *v_ready, *v_free, *q_full;  // pairs (o_full: PV of tile t done)
   uint64_t* o_free;                                         // once per job: O read out, next job may overwrite
   uint64_t* drain;
-  uint64_t* never;  // nothing arrives on it: the abort-path probe waits on it
 };
 
 
@@ -269,19 +269,19 @@ __device__ __forceinline__ float2 combine3x2(const float* v, int r) {
   return ffma2(lo, make_float2(0.00390625f, 0.00390625f), ffma2(mid, make_float2(0.0625f, 0.0625f), hi));
 }
 
-// y0, y1 (0 <= y <= 448) rounded once to f16 and split into three e4m3
-// terms y_h = hi + mid / 16 + lo / 256 in f16 arithmetic: the residuals of an
-// 11-bit value are exact in f16 (Sterbenz) and the three terms hold all of
-// it. Used for P: ten instructions a pair instead of thirteen, at f16
-// precision (relative error <= 2^-12).
-__device__ __forceinline__ void split3x2_h(float2 y, uint16_t& hb, uint16_t& mb, uint16_t& lb) {
-  const __half2 yh = __floats2half2_rn(y.x, y.y);
-  const __half2 k16 = __float2half2_rn(16.f), km16 = __float2half2_rn(-16.f);
-  hb = h2_to_e4m3x2(yh);
-  const __half2 r1 = __hfma2(e4m3x2_to_h2(hb), km16, __hmul2(yh, k16));  // (y - hi) * 16
-  mb = h2_to_e4m3x2(r1);
-  const __half2 r2 = __hfma2(e4m3x2_to_h2(mb), km16, __hmul2(r1, k16));  // (r1 - mid) * 16
-  lb = h2_to_e4m3x2(r2);
+// split3 on a pair with packed residual arithmetic (the residuals are exact):
+// y = hi + mid / 16 + lo / 256, each term e4m3. Used for P (0 <= y <= 448).
+// A variant that first rounds y to f16 (three fewer instructions a pair)
+// measured 4x the output error at the config-3 shape (0.0026 max-abs against
+// the oracle where |o| reaches 13, beyond the 2e-3 tolerance); this one
+// stays at 7e-4.
+__device__ __forceinline__ void split3x2(float2 y, uint16_t& hb, uint16_t& mb, uint16_t& lb) {
+  const float2 m16 = make_float2(-16.f, -16.f), p16 = make_float2(16.f, 16.f);
+  hb = f2_to_e4m3x2(y.x, y.y);
+  const float2 r1 = ffma2(e4m3x2_to_f2(hb), m16, fmul2(y, p16));
+  mb = f2_to_e4m3x2(r1.x, r1.y);
+  const float2 r2 = ffma2(e4m3x2_to_f2(mb), m16, fmul2(r1, p16));
+  lb = f2_to_e4m3x2(r2.x, r2.y);
 }
 
 
@@ -339,7 +339,6 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   b.q_full = b.v_free + 2;
   b.drain = b.q_full + 2;
   b.k_ready = b.drain + 1;
-  b.never = b.k_ready + S;
   float* red_all = reinterpret_cast<float*>(sm + C::RED_OFF);   // [NWG][2][4][NQP]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + C::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + C::MISC_OFF + 4);
@@ -369,7 +368,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       mbar_init(&b.q_full[i], NWG);
     }
     mbar_init(b.drain, 2);  // one commit from each MMA issuer
-    mbar_init(b.never, 1);
+    mbar_init(b.k_ready + S, 1);  // "never": nothing arrives on it (the abort-path probe)
     *abort_flag = 0;
     never_abort = 0;
     fence_mbar_init();
@@ -636,7 +635,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       if (lane == 0) {
         const uint32_t idesc_s = idesc_f8f6f4(Fmt<FMT>::MMA_FMT, 0u, 0u, 0u, (uint32_t)NS);
         // the abort-path probe: a bounded wait on a phase nothing completes
-        bool ok = !a.abort_probe_ns || mbar_wait_rt(b.never, 0, abort_flag, a.abort_probe_ns);
+        bool ok = !a.abort_probe_ns || mbar_wait_rt(b.k_ready + S, 0, abort_flag, a.abort_probe_ns);
         int it = 0, jc = 0;
         for (int p = blockIdx.x; ok && p < total_jobs; p += gridDim.x) {
           int seq, tb, te, split, h, g;
@@ -879,10 +878,14 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             }
           }
           named_bar_sync(bar_id, 128);
+          // lane r < NQP takes row r's maximum over the four warps and hands it
+          // round (rather than every lane loading all 4 x NQP, which the
+          // compiler hoists into as many live registers)
+          const float mine = lane < NQP ? fmaxf(fmaxf(rd[lane], rd[NQP + lane]), fmaxf(rd[2 * NQP + lane], rd[3 * NQP + lane])) : 0.f;
           float cc[NQP];  // correction of each row's earlier sums: 2^(m_old - m_new)
 #pragma unroll
           for (int r = 0; r < NQP; ++r) {
-            const float mt = fmaxf(fmaxf(rd[r], rd[NQP + r]), fmaxf(rd[2 * NQP + r], rd[3 * NQP + r])) - kLog2PScale;
+            const float mt = __shfl_sync(0xffffffffu, mine, r) - kLog2PScale;
             float& mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
             float& lr = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
             cc[r] = 1.f;
@@ -938,7 +941,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           const float2 pv = make_float2(exp2_approx(d.x), exp2_approx(d.y));
           l2[q] = fadd2(l2[q], pv);
           uint16_t hb, mb, lb;
-          split3x2_h(pv, hb, mb, lb);
+          split3x2(pv, hb, mb, lb);
           const int r = 2 * q, sh = 16 * (q & 1);
           w[r >> 2] |= (uint32_t)hb << sh;
           w[(NQP + r) >> 2] |= (uint32_t)mb << sh;

@@ -318,19 +318,6 @@ __device__ __forceinline__ float2 e4m3x2_to_f2(uint16_t v) {
   return __half22float2(h);
 }
 
-// Two f16 (a __half2, low half first) -> two e4m3 bytes (round to nearest
-// even, saturating), and back (exact).
-__device__ __forceinline__ uint16_t h2_to_e4m3x2(__half2 v) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(*reinterpret_cast<uint32_t*>(&v)));
-  return r;
-}
-__device__ __forceinline__ __half2 e4m3x2_to_h2(uint16_t v) {
-  uint32_t h2;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(v));
-  return *reinterpret_cast<__half2*>(&h2);
-}
-
 // ---- packed fp32 pairs (Blackwell f32x2 ALU ops) ---------------------------
 __device__ __forceinline__ uint64_t f2_bits(float2 v) {
   return (uint64_t)__float_as_uint(v.x) | ((uint64_t)__float_as_uint(v.y) << 32);

@@ -15,6 +15,18 @@ from tests.helpers import Case, assert_close_bf16, assert_close_fp32
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _no_tensor_core_fallback():
+    """Every shape the tensor-core kernel takes must find a variant whose
+    register split fits the build: a call that silently ran the CUDA-core
+    decode instead is counted by the library and fails the test."""
+    from mjolnir_b200 import _lib
+
+    before = _lib.load().mj_tc_fallbacks()
+    yield
+    assert _lib.load().mj_tc_fallbacks() == before, "a decode fell back to the CUDA-core kernel"
+
+
 def test_golden_reference_outputs():
     """The kernel on the reference's own fixtures vs the reference's ref_decode output."""
     from mjolnir_b200.runner import DecodeRunner

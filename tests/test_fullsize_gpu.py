@@ -3,9 +3,15 @@ north-star shape), through the public API: one whole step (cache write of the
 step's tokens, decode, split merge) over the full resident workload, then
 the oracle on a sample of it -- a few sequences, each with a couple of KV
 heads, dequantised from the very bytes the write kernel left in the cache.
-A size-independent property rides along: the full batch of outputs is
-finite, and a second step with the same inputs reproduces the first bit for
-bit (the kernels are deterministic).
+Size-independent properties ride along: the full batch of outputs is
+finite, a second step with the same inputs reproduces the first bit for bit
+(the kernels are deterministic), and every output row -- all sequences, all
+heads -- agrees with the CUDA-core kernel's (exact fp32 arithmetic, itself
+checked against the oracle at small sizes) on the same cache, so a fault in
+any work item or head shows, not only in the sampled ones. That comparison
+runs both kernels with fp32 outputs at the fp32 tolerance: two bf16 results
+may sit one bf16 ulp apart (0.03 at |o| = 4, which the V outliers reach)
+when their fp32 values straddle a rounding boundary.
 """
 
 import math
@@ -15,7 +21,7 @@ import pytest
 import torch
 
 from oracle.attention import decode_attention, dequant_pool
-from tests.helpers import assert_close_bf16
+from tests.helpers import assert_close_bf16, assert_close_fp32
 
 pytestmark = pytest.mark.gpu
 
@@ -79,10 +85,26 @@ def _check(wl, workload, kv):
         outs.append(wl.out.clone())
     assert torch.isfinite(outs[0].float()).all()
     assert torch.equal(outs[0], outs[1]), "a repeated step must reproduce its output"
+    # the whole batch against the CUDA-core kernel on the same bytes
+    from mjolnir_b200.runner import DecodeRunner
+
+    simt = DecodeRunner(num_heads=wl.h_q, num_kv_heads=wl.h_k, head_size=wl.d, page_size=wl.PS, max_num_seqs=wl.b,
+                        max_q_len=wl.q_len, kv_format=wl.fmt, device=wl.device, kernel="simt")
+    plan = simt.plan(wl.lens, wl.b, wl.q_len, wl.block_table, wl.seq_lens)
+    f32 = {}
+    for name, r, p in (("tc", wl.runner, wl.plan), ("simt", simt, plan)):
+        f32[name] = torch.empty(wl.out.shape, dtype=torch.float32, device=wl.device)
+        r.run(p, wl.query, f32[name], wl.k_view, wl.v_view, wl.kd, wl.vd, wl.scale, k_scales=wl.k_scales,
+              v_scales=wl.v_scales, q_mul=wl.q_mul, o_mul=wl.o_mul)
+        torch.cuda.synchronize()
+        r.check_status()
+    assert_close_fp32(f32["tc"], f32["simt"], what=f"{workload}/{kv}: every row vs the CUDA-core kernel")
+    assert_close_bf16(outs[0], f32["tc"], what=f"{workload}/{kv}: the bf16 step vs its fp32 output")
+    del f32
     rng = np.random.default_rng(7)
     b = len(wl.lens)
-    seqs = sorted({0, b - 1, int(rng.integers(0, b))})
-    heads = sorted({0, wl.h_k - 1})
+    seqs = sorted({0, b // 2, b - 1, int(rng.integers(0, b))})
+    heads = sorted({0, wl.h_k // 2, wl.h_k - 1})
     ref = _sampled_reference(wl, seqs, heads)
     h_r, ql, d = wl.h_q // wl.h_k, wl.q_len, wl.d
     got = wl.out.view(wl.T, wl.h_q, d)
