@@ -792,15 +792,17 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       if (t == 0) mbar_arrive(&b.q_full[jc & 1]);
       ++jc;
 
-      // Query rows in pairs (packed f32x2 math). m: running max in log2 units,
-      // raised lazily (see kRescaleLog2); l: this thread's partial row sums.
+      // Query rows in pairs (packed f32x2 math). nm: minus the running max m'
+      // in log2 units (raised lazily, see kRescaleLog2), floored so that a row
+      // that has seen no key (m' = -inf) keeps nm = 3e38 and exponents of
+      // -inf (p = 0, not NaN); l: this thread's partial row sums.
       // O accumulates in TMEM over the job's tiles (the PV MMA adds each tile);
       // when a row's max is raised, its O columns are rescaled in place.
       constexpr int NP = NQP / 2;
-      float2 m2[NP], l2[NP];
+      float2 nm2[NP], l2[NP];
 #pragma unroll
       for (int q = 0; q < NP; ++q) {
-        m2[q] = make_float2(-INFINITY, -INFINITY);
+        nm2[q] = make_float2(3.0e38f, 3.0e38f);
         l2[q] = make_float2(0.f, 0.f);
       }
       const float2 c2v = make_float2(c2, c2);
@@ -850,16 +852,24 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         mbar_arrive(&b.s_free[it & 1]);
         const int j0 = (tb + i) * kTileRows, j = j0 + t;  // this thread's KV row
         const bool edge = j0 + kTileRows - 1 > lim_min;  // some row sees only part of this tile
-        bool grow = false;
+        if (edge) {  // rare (the tiles at a causal tail): recompute the limits
 #pragma unroll
-        for (int q = 0; q < NP; ++q) {
-          float2 v = x2[q];
-          if (edge) {  // rare (the tiles at a causal tail): recompute the limits
-            if (j > lim_of(2 * q)) v.x = -INFINITY;
-            if (j > lim_of(2 * q + 1)) v.y = -INFINITY;
+          for (int q = 0; q < NP; ++q) {
+            if (j > lim_of(2 * q)) x2[q].x = -INFINITY;
+            if (j > lim_of(2 * q + 1)) x2[q].y = -INFINITY;
           }
-          x2[q] = v;
-          grow = grow || (v.x > m2[q].x + (kRescaleLog2 + kLog2PScale)) || (v.y > m2[q].y + (kRescaleLog2 + kLog2PScale));
+        }
+        // From here x2 holds the exponents d = s - m'. The job's first tile
+        // always sets the running max; later ones test the largest exponent.
+        bool grow = i == 0;
+        if (!grow) {
+          float dmax = -INFINITY;
+#pragma unroll
+          for (int q = 0; q < NP; ++q) {
+            x2[q] = fadd2(x2[q], nm2[q]);
+            dmax = fmaxf(dmax, fmaxf(x2[q].x, x2[q].y));
+          }
+          grow = dmax > kRescaleLog2 + kLog2PScale;
         }
         // one barrier per tile: a uniform vote on "some score outgrew its row's
         // max" (or abort); only then do the rows exchange their tile maxima
@@ -867,6 +877,10 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           if (named_bar_or(bar_id, 128, *abort_flag != 0)) {
             aborted = true;
             break;
+          }
+          if (i > 0) {  // back to scores: m' is finite here for every row that sees a key
+#pragma unroll
+            for (int q = 0; q < NP; ++q) x2[q] = fadd2(x2[q], make_float2(-nm2[q].x, -nm2[q].y));
           }
           float* rd = red + (it & 1) * 4 * NQP;
 #pragma unroll
@@ -886,13 +900,13 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
 #pragma unroll
           for (int r = 0; r < NQP; ++r) {
             const float mt = __shfl_sync(0xffffffffu, mine, r) - kLog2PScale;
-            float& mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
+            float& nmr = (r & 1) ? nm2[r >> 1].y : nm2[r >> 1].x;
             float& lr = (r & 1) ? l2[r >> 1].y : l2[r >> 1].x;
             cc[r] = 1.f;
-            if (mt > mr) {
-              cc[r] = mr == -INFINITY ? 0.f : exp2_approx(mr - mt);
+            if (mt > -nmr) {  // from a row with no key yet (nm = 3e38): 2^-inf = 0
+              cc[r] = exp2_approx(-nmr - mt);
               lr *= cc[r];
-              mr = mt;
+              nmr = -mt;
             }
           }
           if (i >= 1) {  // O holds tiles tb .. tb+i-1: once PV_{it-1} lands, scale its rows
@@ -925,6 +939,8 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             }
             tmem_wait_st();
           }
+#pragma unroll
+          for (int q = 0; q < NP; ++q) x2[q] = fadd2(x2[q], nm2[q]);  // exponents under the new max
         }
         // P: three e4m3 terms per row, this thread's KV row s = t packed as the
         // 16-byte row s of each MN-major group (N rows hi | mid | lo | padding)
@@ -935,10 +951,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
         for (int k = 0; k < NW; ++k) w[k] = 0u;
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
-          // a row that has seen no key keeps m = -inf and all its scores -inf:
-          // the floor makes their exponent -inf (p = 0) instead of NaN
-          const float2 d = fadd2(x2[q], make_float2(-fmaxf(m2[q].x, -3.0e38f), -fmaxf(m2[q].y, -3.0e38f)));
-          const float2 pv = make_float2(exp2_approx(d.x), exp2_approx(d.y));
+          const float2 pv = make_float2(exp2_approx(x2[q].x), exp2_approx(x2[q].y));
           l2[q] = fadd2(l2[q], pv);
           uint16_t hb, mb, lb;
           split3x2(pv, hb, mb, lb);
@@ -1056,7 +1069,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           for (int r = 0; r < NQP; ++r)
             if (r == t) {
               lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
-              mr = (r & 1) ? m2[r >> 1].y : m2[r >> 1].x;
+              mr = -((r & 1) ? nm2[r >> 1].y : nm2[r >> 1].x);
             }
           const float lse = lt > 0.f ? (mr + log2f(lt)) * kLn2 : -INFINITY;
           if (!final_out) a.lse_part[(((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + row0 + t] = lse;
