@@ -327,3 +327,36 @@ def test_bounded_wait_runs_out_and_the_next_call_is_exact(kv_format, q_len, h_q)
     out, _, _ = c.run(kernel="tc")
     ref, _ = c.oracle()
     assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref, what=f"{kv_format} q_len {q_len} after a timed-out launch")
+
+
+def test_reset_after_an_error_clears_stale_merge_counts():
+    """In-kernel split merge after a device error: a job that stopped early
+    never counts itself in, so counters can be left short of a full count.
+    check_status clears them with the status word; the same runner and plan
+    then merge correctly. The counters are dirtied by hand after a timed-out
+    launch (the probe stops every job before it counts)."""
+    from mjolnir_b200 import _lib
+    from mjolnir_b200.runner import _stream
+
+    c = Case(seq_lens=(6000, 2500, 700), h_q=32, h_k=8, kv_format="e2m3", seed=34, outliers=0.01)
+    r = c.runner(fused_merge=True, kernel="tc")
+    plan = r.plan(c.seq_lens, c.b, 1, c.block_table, c.seq_lens_t)
+    assert plan.with_reduction and int(plan.n_splits.max()) <= 16
+    scale = 1.0 / math.sqrt(c.d)
+    kd, vd, qm, om = c.dev(c.kd), c.dev(c.vd), c.dev(c.q_mul), c.dev(c.o_mul)
+    out = torch.zeros(c.b, c.h_q * c.d, device="cuda")
+    args = r.decode_args(plan, c.query, out, c.k_view, c.v_view, kd, vd, scale, q_mul=qm, o_mul=om)
+    args.abort_probe_ns = 2000
+    _lib.decode(args, _stream())
+    torch.cuda.synchronize()
+    r.merge_counters.fill_(1)
+    with pytest.raises(_lib.MjolnirError, match=f"device status {_lib.MJ_DEV_TIMEOUT}"):
+        r.check_status()
+    assert int(r.merge_counters.abs().sum()) == 0 and int(r.status.item()) == 0
+    got = torch.full((c.b, c.h_q * c.d), float("nan"), device="cuda")
+    r.run(plan, c.query, got, c.k_view, c.v_view, kd, vd, scale, q_mul=qm, o_mul=om)
+    torch.cuda.synchronize()
+    r.check_status()
+    ref, _ = c.oracle()
+    assert_close_fp32(got.view(c.b, c.h_q, c.d), ref, what="in-kernel merge after a reset")
+    assert int(r.merge_counters.abs().sum()) == 0
