@@ -53,6 +53,9 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#ifndef MJ_NVFP4_SMV
+#define MJ_NVFP4_SMV 1
+#endif
 #ifndef MJ_CVT_BALANCED
 #define MJ_CVT_BALANCED 1
 #endif
@@ -181,6 +184,10 @@ struct Cfg {
   static constexpr int CVT_BASE = (MJ_CVT_BALANCED && CVTW) ? 0 : 32;  // converter index of the warpgroup's thread 0
   static constexpr bool SM_CONVERTS = Fmt<FMT>::NARROW && CVTW == 0;  // softmax warpgroups share the conversion
   static constexpr int CVT_THREADS = CVT_ROLE + (SM_CONVERTS ? 128 * NWG : 0);  // threads that convert a V tile
+  // nvfp4 at 4 rows per KV head: the converter warpgroup converts K (on the
+  // S MMA's path), the softmax warpgroup converts V after publishing P (ns
+  // shape +5 %; at 8 rows the softmax has no room for it: -10 %)
+  static constexpr bool SM_CVT_V = MJ_NVFP4_SMV && Fmt<FMT>::SCALED && NWG == 1 && NQP <= 4;
   // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
   // warpgroup w owns rows w * NQP .. of each block.
   static constexpr int NS = (3 * RT + 7) / 8 * 8 < 16 ? 16 : (3 * RT + 7) / 8 * 8;  // S MMA N (Q is K-major)
@@ -363,7 +370,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       if (i == 0) mbar_init(b.o_free, 128 * NWG);
       // narrow formats: the converter role (and, without a converter
       // warpgroup, the softmax warpgroups) share the V conversion
-      mbar_init(&b.v_ready[i], Fmt<FMT>::NARROW ? C::CVT_THREADS : C::CVT_ROLE);
+      mbar_init(&b.v_ready[i], C::SM_CVT_V ? 128 : Fmt<FMT>::NARROW ? C::CVT_THREADS : C::CVT_ROLE);
       mbar_init(&b.v_free[i], 1);
       mbar_init(&b.q_full[i], NWG);
     }
@@ -476,6 +483,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           nvfp4_tile(kbuf(st), kscl(st), valid, ct, C::CVT_ROLE);
           fence_proxy_async_smem();
           mbar_arrive(&b.k_ready[st]);
+          if constexpr (C::SM_CVT_V) continue;
           ok = (FUSED || mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, wait_ns)) &&
                mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, wait_ns);
           if (!ok) break;
@@ -989,6 +997,12 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
             *q = Fmt<FMT>::convert(*q);
           }
+          fence_proxy_async_smem();
+          mbar_arrive(&b.v_ready[it & 1]);
+        } else if constexpr (C::SM_CVT_V) {  // nvfp4: this tile's V, rows past the sequence zeroed
+          const int st = it % S;
+          if (!FUSED && !mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, wait_ns) && !*abort_flag) give_up();
+          nvfp4_tile(vbuf(st), vscl(st), L - j0, t, 128);
           fence_proxy_async_smem();
           mbar_arrive(&b.v_ready[it & 1]);
         }
