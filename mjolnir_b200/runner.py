@@ -57,6 +57,7 @@ class StepPlan:
     chunk_tiles: int
     num_chunks: int
     causal: bool = True
+    tile_jobs: int = 0  # 128-row KV tiles x KV heads the step reads
 
 
 # ---------------------------------------------------------------------------
@@ -290,11 +291,15 @@ class DecodeRunner:
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         # split merge inside the tensor-core kernel (its last job per sequence
         # and KV head merges; the counters return to zero after every launch).
-        # Off by default: it saves the combine launch but its fences, atomics
-        # and serial merges at the ends of jobs cost more on B200 (cfg2 decode
-        # 96 % -> 73 % of HBM, cfg3 81 % -> 74 %); MJOLNIR_ATTN_FUSED_MERGE=1.
+        # It saves the combine launch, which pays on short steps (fp8, batch 4
+        # x 4K: 30 -> 21 us per step), but its fences, atomics and serial
+        # merges at the ends of jobs cost more on long ones (cfg2 -25 %, cfg3
+        # and the north-star shape -9 %). None (MJOLNIR_ATTN_FUSED_MERGE=auto,
+        # the default) decides per plan: in the kernel when the step reads at
+        # most 16 tiles per SM; 1 / 0 force it on / off.
         if fused_merge is None:
-            fused_merge = env_flag("MJOLNIR_ATTN_FUSED_MERGE", "0").lower() in ("1", "true", "yes")
+            mode = env_flag("MJOLNIR_ATTN_FUSED_MERGE", "auto").lower()
+            fused_merge = True if mode in ("1", "true", "yes") else False if mode in ("0", "false", "no") else None
         self.fused_merge = fused_merge
         self.merge_counters = torch.zeros(max_num_seqs * self.h_k * 64, dtype=torch.int32, device=dev)
         self._one = torch.ones(1, dtype=torch.float32, device=dev)
@@ -366,6 +371,7 @@ class DecodeRunner:
             chunk_tiles=p.chunk_tiles,
             num_chunks=real,
             causal=causal or q_len == 1,
+            tile_jobs=sum(-(-L // 128) for L in lens) * self.h_k,
         )
 
     # ---------------------------------------------------------------- launch
@@ -429,9 +435,15 @@ class DecodeRunner:
         a.with_combine = int(plan.with_reduction)
         a.kernel = self.kernel
         a.status = self.status.data_ptr()
-        a.merge_counters = self.merge_counters.data_ptr() if self.fused_merge else None
+        a.merge_counters = self.merge_counters.data_ptr() if self.merges(plan) else None
         set_scale_views(a, k_scales, v_scales, k_cache.shape[0], self.page_size, self.h_k, self.d, self.kv_format)
         return a
+
+    def merges(self, plan: StepPlan) -> bool:
+        """Whether this plan's launches carry the in-kernel merge counters."""
+        if self.fused_merge is not None:
+            return bool(self.fused_merge)
+        return plan.tile_jobs <= 16 * self.sm_count
 
     def merges_in_kernel(self, args: _lib.DecodeArgs) -> bool:
         """True when mj_decode merges the split partials inside the decode

@@ -46,7 +46,7 @@ def _decode_both(c, runner, plan, out_dtype=torch.float32):
 def test_noalloc_matches_decode_two_calls_in_a_row():
     # 148 SMs and 3 sequences: every sequence splits, so the partials are used
     first = Case(seq_lens=(5000, 3000, 129), h_q=32, h_k=8, kv_format="e2m3", seed=21, outliers=0.01)
-    r1 = first.runner()
+    r1 = first.runner(fused_merge=False)  # partials merged by the combine launch (the next test: in the kernel)
     p1 = r1.plan(first.seq_lens, first.b, 1, first.block_table, first.seq_lens_t)
     assert p1.with_reduction
     ref1, got1 = _decode_both(first, r1, p1)
@@ -54,7 +54,7 @@ def test_noalloc_matches_decode_two_calls_in_a_row():
     # a second call with other shapes and data right after the first: the
     # array still holds call 1's partials, which must not leak into call 2
     second = Case(seq_lens=(2100, 40, 7000, 900), q_len=2, h_q=16, h_k=2, kv_format="fp8", seed=22, descale="head")
-    r2 = second.runner()
+    r2 = second.runner(fused_merge=False)
     p2 = r2.plan(second.seq_lens, second.b, 2, second.block_table, second.seq_lens_t)
     assert p2.with_reduction
     ref2, got2 = _decode_both(second, r2, p2)
