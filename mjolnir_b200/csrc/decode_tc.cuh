@@ -115,15 +115,21 @@ __device__ __forceinline__ uint4 e3m2x16_to_e4m3(uint4 raw) {
 }
 
 // e2m1: a 16U4 slot holds 16 nibbles in its first 8 bytes; code s|e|m becomes
-// byte s<<7 | e<<3 | m<<2, value * 2^-6 (subnormals included).
-__device__ __forceinline__ uint32_t e2m1_bytes(uint32_t nib4) {  // 4 codes, one per byte (low nibbles)
-  return ((nib4 & 0x07070707u) << 2) | ((nib4 & 0x08080808u) << 4);
+// byte s<<7 | e<<3 | m<<2, value * 2^-6 (subnormals included). The even
+// codes (low nibbles) and the odd ones (high nibbles) of a word become e4m3
+// bytes where they sit, then one byte permute per output word interleaves
+// them.
+__device__ __forceinline__ uint32_t e2m1_even_bytes(uint32_t w) {
+  return ((w & 0x07070707u) << 2) | ((w & 0x08080808u) << 4);
+}
+__device__ __forceinline__ uint32_t e2m1_odd_bytes(uint32_t w) {
+  return ((w >> 2) & 0x1C1C1C1Cu) | (w & 0x80808080u);
 }
 __device__ __forceinline__ uint4 e2m1x16_to_e4m3(uint4 raw) {
-  const uint32_t e0 = raw.x & 0x0F0F0F0Fu, o0 = (raw.x >> 4) & 0x0F0F0F0Fu;
-  const uint32_t e1 = raw.y & 0x0F0F0F0Fu, o1 = (raw.y >> 4) & 0x0F0F0F0Fu;
-  return make_uint4(e2m1_bytes(__byte_perm(e0, o0, 0x5140)), e2m1_bytes(__byte_perm(e0, o0, 0x7362)),
-                    e2m1_bytes(__byte_perm(e1, o1, 0x5140)), e2m1_bytes(__byte_perm(e1, o1, 0x7362)));
+  const uint32_t e0 = e2m1_even_bytes(raw.x), o0 = e2m1_odd_bytes(raw.x);
+  const uint32_t e1 = e2m1_even_bytes(raw.y), o1 = e2m1_odd_bytes(raw.y);
+  return make_uint4(__byte_perm(e0, o0, 0x5140), __byte_perm(e0, o0, 0x7362), __byte_perm(e1, o1, 0x5140),
+                    __byte_perm(e1, o1, 0x7362));
 }
 
 // nvfp4: 8 e2m1 codes (nibbles of w, code 0 lowest) -> 8 e4m3 bytes
