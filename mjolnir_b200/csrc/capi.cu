@@ -173,8 +173,10 @@ int mj_decode(const mj_decode_args* args, void* stream) {
     e = mj::launch_decode_simt(a, s);
     if (e != cudaSuccess) return cuda_status(e, "mj_decode launch");
   }
-  // the one-warpgroup tensor-core variants merge in the kernel when given counters
-  const bool merged = handled && a.merge_counters && a.q_len * (a.h_q / a.h_k) <= 16 && a.max_splits <= 16;
+  // the one-warpgroup tensor-core variants (every head_dim-256 one) merge in
+  // the kernel when given counters
+  const bool merged = handled && a.merge_counters && (a.q_len * (a.h_q / a.h_k) <= 16 || a.head_size == 256) &&
+                      a.max_splits <= 16;
   if (a.with_combine && !merged) {
     if (!a.o_part) return fail(MJ_ERR_INVALID, "mj_decode: with_combine needs partial buffers");
     return cuda_status(mj::launch_combine(a, s), "mj_combine launch");

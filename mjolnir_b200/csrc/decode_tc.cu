@@ -54,7 +54,8 @@ const char* tc_ineligible(const mj_decode_args& a) {
     for (int i = 0; i < 6; ++i)
       if (ss[i] % 8) return "nvfp4 scale stride alignment";
   }
-  if (a.head_size != 128) return "head_size != 128";
+  if (a.head_size != 128 && a.head_size != 256) return "head_size not 128 or 256";
+  if (a.head_size == 256 && a.kv_format == MJ_KV_NVFP4) return "nvfp4 at head_size 256";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";
   const uintptr_t al = a.kv_format == MJ_KV_FP8_E4M3 ? 16 : 32;
@@ -75,20 +76,34 @@ static CUtensorMapDataType tma_type(int kv_format) {
   return CU_TENSOR_MAP_DATA_TYPE_UINT8;
 }
 
+// One operand's rows as (codes, page_size rows, h_k, pages) boxes of one
+// page; head_dim 256 adds a dimension of the two 128-code halves of a row
+// (codes, half, rows, h_k, pages), one box per half.
 static bool make_map(CUtensorMap* m, const void* base, int64_t s_page, int64_t s_row, int64_t s_head,
                      const mj_decode_args& a) {
   const bool narrow = a.kv_format != MJ_KV_FP8_E4M3;
   // a dimension of extent 1 never moves its coordinate; give it any legal stride
   const int64_t fill = narrow ? 32 : 16;
-  cuuint64_t dims[4] = {128, (cuuint64_t)a.page_size, (cuuint64_t)a.h_k, (cuuint64_t)a.num_pages};
-  cuuint64_t strides[3] = {(cuuint64_t)(s_row ? s_row : fill), (cuuint64_t)(s_head ? s_head : fill),
-                           (cuuint64_t)(s_page ? s_page : fill)};
-  cuuint32_t box[4] = {128, (cuuint32_t)a.page_size, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = encode_fn()(m, tma_type(a.kv_format), 4,
-                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const cuuint64_t sr = (cuuint64_t)(s_row ? s_row : fill), sh = (cuuint64_t)(s_head ? s_head : fill),
+                   sp = (cuuint64_t)(s_page ? s_page : fill);
+  CUresult r;
+  if (a.head_size == 256) {
+    cuuint64_t dims[5] = {128, 2, (cuuint64_t)a.page_size, (cuuint64_t)a.h_k, (cuuint64_t)a.num_pages};
+    cuuint64_t strides[4] = {(cuuint64_t)mj_row_bytes(128, a.kv_format), sr, sh, sp};
+    cuuint32_t box[5] = {128, 1, (cuuint32_t)a.page_size, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    r = encode_fn()(m, tma_type(a.kv_format), 5, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[4] = {128, (cuuint64_t)a.page_size, (cuuint64_t)a.h_k, (cuuint64_t)a.num_pages};
+    cuuint64_t strides[3] = {sr, sh, sp};
+    cuuint32_t box[4] = {128, (cuuint32_t)a.page_size, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = encode_fn()(m, tma_type(a.kv_format), 4, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   return r == CUDA_SUCCESS;
 }
 
@@ -100,7 +115,7 @@ static bool make_map(CUtensorMap* m, const void* base, int64_t s_page, int64_t s
 // 5-D box -- (codes, 8 rows, K|V, row groups, page * h_k + head) -- loads a
 // page's K and V at once: half the TMA operations of separate boxes.
 static bool fused_layout(const mj_decode_args& a, int64_t* pagehead_stride) {
-  const int64_t rb = mj_row_bytes(128, a.kv_format);
+  const int64_t rb = mj_row_bytes(a.head_size, a.kv_format);
   if ((uintptr_t)a.v_cache != (uintptr_t)a.k_cache + (uintptr_t)rb) return false;
   if (a.k_stride_page != a.v_stride_page || a.k_stride_row != a.v_stride_row || a.k_stride_head != a.v_stride_head)
     return false;
@@ -114,16 +129,19 @@ static bool fused_layout(const mj_decode_args& a, int64_t* pagehead_stride) {
   return *pagehead_stride >= (int64_t)a.page_size * a.k_stride_row;
 }
 
-static bool make_map_fused(CUtensorMap* m, const mj_decode_args& a, int64_t pagehead_stride) {
-  const int64_t rb = mj_row_bytes(128, a.kv_format);
+// head_dim 256: one map per 128-code half of the rows (half 1 starts half a
+// row further on), each box the K and V half-rows of one page.
+static bool make_map_fused(CUtensorMap* m, const mj_decode_args& a, int64_t pagehead_stride, int half) {
+  const int64_t rb = mj_row_bytes(a.head_size, a.kv_format);
   const int64_t heads = a.h_k > 1 ? a.h_k : 1;
+  const unsigned char* base = static_cast<const unsigned char*>(a.k_cache) + half * mj_row_bytes(128, a.kv_format);
   cuuint64_t dims[5] = {128, 8, 2, (cuuint64_t)(a.page_size / 8), (cuuint64_t)(a.num_pages * heads)};
   cuuint64_t strides[4] = {(cuuint64_t)a.k_stride_row, (cuuint64_t)rb, (cuuint64_t)(8 * a.k_stride_row),
                            (cuuint64_t)pagehead_stride};
   cuuint32_t box[5] = {128, 8, 2, (cuuint32_t)(a.page_size / 8), 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = encode_fn()(m, tma_type(a.kv_format), 5,
-                           const_cast<void*>(a.k_cache), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           const_cast<unsigned char*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -152,8 +170,12 @@ cudaError_t launch_decode_tc(const mj_decode_args& a, cudaStream_t stream, bool*
   int64_t ph_stride = 0;
   const bool fused = fused_layout(a, &ph_stride);
   if (fused) {
-    if (!make_map_fused(&mk, a, ph_stride)) return cudaErrorInvalidValue;
-    mv = mk;  // unused
+    if (!make_map_fused(&mk, a, ph_stride, 0)) return cudaErrorInvalidValue;
+    if (a.head_size == 256) {
+      if (!make_map_fused(&mv, a, ph_stride, 1)) return cudaErrorInvalidValue;
+    } else {
+      mv = mk;  // unused
+    }
   } else if (!make_map(&mk, a.k_cache, a.k_stride_page, a.k_stride_row, a.k_stride_head, a) ||
              !make_map(&mv, a.v_cache, a.v_stride_page, a.v_stride_row, a.v_stride_head, a)) {
     return cudaErrorInvalidValue;

@@ -176,13 +176,17 @@ struct Fmt {
 // A CTA runs NWG softmax warpgroups of NQP query rows each (RT = NWG * NQP
 // rows per job). One warpgroup: two CTAs per SM; several: one CTA per SM that
 // streams each KV tile once for all its rows. CVTW = 1 adds a warpgroup of
-// converter warps so that the softmax warpgroup converts no V.
-template <int FMT, int NQP, int NWG, int CVTW>
+// converter warps so that the softmax warpgroup converts no V. DH = 2 runs
+// head_dim 256 as two 128-wide halves: each stage holds both halves of K and
+// V, S sums 8 K-steps, O is two TMEM blocks (one per half), each softmax
+// thread owns head-dim elements t and 128 + t; one CTA per SM.
+template <int FMT, int NQP, int NWG, int CVTW, int DH = 1>
 struct Cfg {
+  static_assert(DH == 1 || (DH == 2 && NWG == 1 && !Fmt<FMT>::SCALED), "head_dim 256: one warpgroup, no nvfp4");
   static constexpr int RT = NWG * NQP;
   static constexpr int SM0 = 4 * (1 + CVTW);             // first softmax warp
   static constexpr int THREADS = 128 * (1 + CVTW + NWG);
-  static constexpr int CTAS_PER_SM = NWG == 1 ? 2 : 1;
+  static constexpr int CTAS_PER_SM = NWG == 1 && DH == 1 ? 2 : 1;
   // threads of the converter role: warp 2, or (MJ_CVT_BALANCED) with a
   // converter warpgroup that warpgroup alone, one converter warp per SM
   // sub-partition beside each softmax warp
@@ -201,9 +205,11 @@ struct Cfg {
   static constexpr int QBYTES = NS * 128;                // one K-major Q operand
   static constexpr int PBYTES = NO * 128;                // one MN-major P operand: NO/16 groups of [128 s][16 B]
   // (nvfp4 at 8 rows: its scale copies leave room for two stages at two CTAs per SM)
-  static constexpr int STAGES = NWG == 1 ? (NQP <= 4 || (NQP == 8 && !Fmt<FMT>::SCALED) ? 3 : 2) : NWG == 2 ? 5 : 4;
+  static constexpr int STAGES = DH == 2 ? (NQP <= 8 ? 3 : 2)
+                               : NWG == 1 ? (NQP <= 4 || (NQP == 8 && !Fmt<FMT>::SCALED) ? 3 : 2) : NWG == 2 ? 5 : 4;
+  static_assert(DH == 1 || !SM_CONVERTS, "head_dim 256: narrow formats convert on a converter warpgroup");
   static_assert(!Fmt<FMT>::SCALED || CVTW == 1, "nvfp4 converts K on the converter warpgroup only");
-  static constexpr int TCOLS = 2 * NS + NO;              // S0 S1 O (O accumulates over a job's tiles)
+  static constexpr int TCOLS = 2 * NS + DH * NO;         // S0 S1 O (O accumulates over a job's tiles; DH blocks)
   static constexpr int TMEM_COLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
   static_assert(TCOLS * CTAS_PER_SM <= 512, "the CTAs of an SM share its 512 TMEM columns");
   static_assert(NWG == 1 || NQP % 16 == 0, "several warpgroups write whole 16-row P groups");
@@ -212,15 +218,15 @@ struct Cfg {
   // two: 80): the TMA / MMA / converter warpgroups keep REG_LO, the softmax
   // ones get REG_HI. REG_POOL must fit THREADS x the launch registers (checked
   // on the host before the first launch).
-  static constexpr int REG_LO = NWG == 3 ? (CVTW ? 48 : 64) : CVTW ? 56 : 0;
-  static constexpr int REG_HI = NWG == 3 ? (CVTW ? 128 : 144) : CVTW ? 128 : 0;
+  static constexpr int REG_LO = DH == 2 ? 0 : NWG == 3 ? (CVTW ? 48 : 64) : CVTW ? 56 : 0;
+  static constexpr int REG_HI = DH == 2 ? 0 : NWG == 3 ? (CVTW ? 128 : 144) : CVTW ? 128 : 0;
   static constexpr int REG_POOL = 128 * REG_LO * (1 + CVTW) + 128 * NWG * REG_HI;
   static constexpr uint32_t K_TX = 128u * Fmt<FMT>::ROW;  // bytes TMA reads per tile operand
   // shared memory plan (offsets from the 1024-aligned dynamic shared memory base)
   static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = K_OFF + STAGES * kTileBytes;
-  static constexpr int Q_OFF = V_OFF + STAGES * kTileBytes;  // two slots (jobs)
-  static constexpr int P_OFF = (Q_OFF + 2 * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
+  static constexpr int V_OFF = K_OFF + STAGES * DH * kTileBytes;
+  static constexpr int Q_OFF = V_OFF + STAGES * DH * kTileBytes;  // two slots (jobs) x DH halves
+  static constexpr int P_OFF = (Q_OFF + 2 * DH * QBYTES + 1023) / 1024 * 1024;  // two slots (tiles)
   static constexpr int BAR_OFF = P_OFF + 2 * PBYTES;
   static constexpr int NBARS = 5 * STAGES + 2 * 8 + 2;  // k/v full/empty rings, k_ready ring, 8 pairs, drain, never
   // float red[NWG][2][4][NQP], 16-byte aligned so its rows load as float4
@@ -308,11 +314,14 @@ namespace tc {
 // (pages, h_k, page_size, K row | V row)); the box lands as alternating 1 KB
 // K and V swizzle atoms, so both operands see an atom stride of 2048 B.
 // Otherwise K and V are separate boxes into separate tiles (atom stride 1024 B).
-template <int FMT, int NQP, int NWG, int CVTW, bool FUSED>
-__global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQP, NWG, CVTW>::CTAS_PER_SM)
+// Head_dim 256 (DH = 2): every box is one 128-code half of the rows (fused:
+// tmk maps half 0, tmv half 1; otherwise a halves dimension in each map).
+template <int FMT, int NQP, int NWG, int CVTW, bool FUSED, int DH>
+__global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT, NQP, NWG, CVTW, DH>::CTAS_PER_SM)
     decode_tc_kernel(const __grid_constant__ mj_decode_args a, const __grid_constant__ CUtensorMap tmk,
                      const __grid_constant__ CUtensorMap tmv) {
-  using C = Cfg<FMT, NQP, NWG, CVTW>;
+  using C = Cfg<FMT, NQP, NWG, CVTW, DH>;
+  constexpr int D = 128 * DH;  // head_dim
   constexpr int NS = C::NS, NO = C::NO, RT = C::RT;
   constexpr int S = C::STAGES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -423,11 +432,15 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
   if (a.with_combine) griddep_launch_dependents();
 
   constexpr uint32_t ATOM = FUSED ? 2048u : 1024u;  // byte stride between 8-row swizzle atoms of K (or V)
-  auto kbuf = [&](int st) { return FUSED ? sm + st * 2 * kTileBytes : sm + C::K_OFF + st * kTileBytes; };
-  auto vbuf = [&](int st) { return FUSED ? sm + st * 2 * kTileBytes + 1024 : sm + C::V_OFF + st * kTileBytes; };
+  auto kbuf = [&](int st, int dh = 0) {
+    return FUSED ? sm + (st * DH + dh) * 2 * kTileBytes : sm + C::K_OFF + (st * DH + dh) * kTileBytes;
+  };
+  auto vbuf = [&](int st, int dh = 0) {
+    return FUSED ? sm + (st * DH + dh) * 2 * kTileBytes + 1024 : sm + C::V_OFF + (st * DH + dh) * kTileBytes;
+  };
   // byte offset of 16-byte chunk c (row c / 8) of the V tile, and of row r
   auto vchunk = [&](int c) { return (uint32_t)((c >> 6) * ATOM + (c & 63) * 16); };
-  auto qbuf = [&](int i) { return sm + C::Q_OFF + i * C::QBYTES; };
+  auto qbuf = [&](int i, int dh = 0) { return sm + C::Q_OFF + (i * DH + dh) * C::QBYTES; };
   auto kscl = [&](int st) { return sm + C::SC_OFF + st * 2048; };  // nvfp4 K scale rows of a stage
   auto vscl = [&](int st) { return sm + C::SC_OFF + st * 2048 + 1024; };
   auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::PBYTES; };
@@ -507,11 +520,14 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           // this role converts chunks ct, ct + CVT_THREADS, ...; without a
           // converter warpgroup the softmax warpgroups convert the others
           // after publishing P
-          unsigned char* vb = vbuf(st);
+#pragma unroll
+          for (int dh = 0; dh < DH; ++dh) {
+            unsigned char* vb = vbuf(st, dh);
 #pragma unroll 2
-          for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
-            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
-            *q = Fmt<FMT>::convert(*q);
+            for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
+              uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+              *q = Fmt<FMT>::convert(*q);
+            }
           }
           // narrow formats have no NaN code: rows past the sequence end are finite and get P = 0
         } else {
@@ -520,9 +536,11 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           const int valid = L - tile * kTileRows;
           if (valid < kTileRows) {
             const int r0 = valid > 0 ? valid : 0;
-            unsigned char* vb = vbuf(st);
-            for (int c = r0 * 8 + ct; c < kTileRows * 8; c += C::CVT_ROLE)
-              *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
+            for (int dh = 0; dh < DH; ++dh) {
+              unsigned char* vb = vbuf(st, dh);
+              for (int c = r0 * 8 + ct; c < kTileRows * 8; c += C::CVT_ROLE)
+                *reinterpret_cast<uint4*>(vb + vchunk(c)) = make_uint4(0, 0, 0, 0);
+            }
           }
         }
         fence_proxy_async_smem();
@@ -594,9 +612,14 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           if (FUSED) {  // one box per page: K and V rows together (the stage frees after PV)
             if (lane == 0) go = mbar_wait(&b.v_empty[st], par, abort_flag, wait_ns);
             if (!__shfl_sync(0xffffffffu, go, 0)) return false;
-            if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * C::K_TX);
+            if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], 2 * DH * C::K_TX);
             __syncwarp();
-            if (lane < P) tma_load_5d(kbuf(st) + lane * PS * 256, &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h, kv_policy);
+            if (lane < P) {
+#pragma unroll
+              for (int dh = 0; dh < DH; ++dh)
+                tma_load_5d(kbuf(st, dh) + lane * PS * 256, dh ? &tmv : &tmk, &b.k_full[st], 0, 0, 0, 0, pg * h_k + h,
+                            kv_policy);
+            }
             if constexpr (Fmt<FMT>::SCALED) {
               copy_scales(tile, pg, st, false);
               copy_scales(tile, pg, st, true);
@@ -607,9 +630,15 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           }
           if (lane == 0) go = mbar_wait(&b.k_empty[st], par, abort_flag, wait_ns);
           if (!__shfl_sync(0xffffffffu, go, 0)) return false;
-          if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], C::K_TX);
+          if (lane == 0) mbar_arrive_expect_tx(&b.k_full[st], DH * C::K_TX);
           __syncwarp();
-          if (lane < P) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg, kv_policy);
+          if (lane < P) {
+            if constexpr (DH == 1) tma_load_4d(kbuf(st) + lane * PS * 128, &tmk, &b.k_full[st], 0, 0, h, pg, kv_policy);
+            else
+#pragma unroll
+              for (int dh = 0; dh < DH; ++dh)
+                tma_load_5d(kbuf(st, dh) + lane * PS * 128, &tmk, &b.k_full[st], 0, dh, 0, h, pg, kv_policy);
+          }
           if constexpr (Fmt<FMT>::SCALED) {
             copy_scales(tile, pg, st, false);
             cp_async_arrive_noinc(&b.k_full[st]);
@@ -617,9 +646,15 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
           k_issued = it + 1;
           if (lane == 0) go = mbar_wait(&b.v_empty[st], par, abort_flag, wait_ns);
           if (!__shfl_sync(0xffffffffu, go, 0)) return false;
-          if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], C::K_TX);
+          if (lane == 0) mbar_arrive_expect_tx(&b.v_full[st], DH * C::K_TX);
           __syncwarp();
-          if (lane < P) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg, kv_policy);
+          if (lane < P) {
+            if constexpr (DH == 1) tma_load_4d(vbuf(st) + lane * PS * 128, &tmv, &b.v_full[st], 0, 0, h, pg, kv_policy);
+            else
+#pragma unroll
+              for (int dh = 0; dh < DH; ++dh)
+                tma_load_5d(vbuf(st, dh) + lane * PS * 128, &tmv, &b.v_full[st], 0, dh, 0, h, pg, kv_policy);
+          }
           if constexpr (Fmt<FMT>::SCALED) {
             copy_scales(tile, pg, st, true);
             cp_async_arrive_noinc(&b.v_full[st]);
@@ -664,12 +699,15 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
                  mbar_wait(&b.s_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, wait_ns);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t kaddr = smem_addr(kbuf(st));
             const uint32_t d = tmem + (uint32_t)((it & 1) * NS);
   #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qaddr + 32 * k, 16, 1024), idesc_s,
-                         k > 0);
+            for (int dh = 0; dh < DH; ++dh) {
+              const uint32_t kaddr = smem_addr(kbuf(st, dh)), qa = qaddr + (uint32_t)(dh * C::QBYTES);
+  #pragma unroll
+              for (int k = 0; k < 4; ++k)
+                mma_f8f6f4(d, smem_desc_sw128(kaddr + 32 * k, 16, ATOM), smem_desc_sw128(qa + 32 * k, 16, 1024), idesc_s,
+                           dh > 0 || k > 0);
+            }
             mma_commit(&b.s_full[it & 1]);
             if (!FUSED) mma_commit(&b.k_empty[st]);  // K is consumed once S is computed
           }
@@ -698,15 +736,19 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
                  mbar_wait(&b.v_ready[it & 1], (it >> 1) & 1, abort_flag, wait_ns);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t vaddr = smem_addr(vbuf(st));
             const uint32_t paddr = smem_addr(pbuf(it & 1));
-            const uint32_t d = tmem + (uint32_t)(2 * NS);
             // P^T is [128 s][16 B] per group of 16 rows: 8-row core matrices 128 B
-            // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows
+            // apart along s (LBO), groups 2048 B apart (SBO); k-step = 32 s-rows.
+            // Head-dim half dh accumulates into its own O block.
   #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_f8f6f4(d, smem_desc_sw128(vaddr + 4 * ATOM * k, kTileBytes, ATOM), smem_desc_noswz(paddr + 512 * k, 128, 2048),
-                         idesc_o, k > 0 || tile > tb);
+            for (int dh = 0; dh < DH; ++dh) {
+              const uint32_t vaddr = smem_addr(vbuf(st, dh));
+              const uint32_t d = tmem + (uint32_t)(2 * NS + dh * NO);
+  #pragma unroll
+              for (int k = 0; k < 4; ++k)
+                mma_f8f6f4(d, smem_desc_sw128(vaddr + 4 * ATOM * k, kTileBytes, ATOM),
+                           smem_desc_noswz(paddr + 512 * k, 128, 2048), idesc_o, k > 0 || tile > tb);
+            }
             mma_commit(&b.o_full[it & 1]);
             mma_commit(&b.v_empty[st]);
             mma_commit(&b.v_free[it & 1]);
@@ -739,7 +781,8 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
     // Q rows past 3*RT (padding to the MMA's N) stay zero for the whole kernel
     if (sw == 0)
       for (int i = 0; i < 2; ++i)
-        for (int row = 3 * RT; row < NS; ++row) qbuf(i)[sw128_offset(row, t)] = 0;
+        for (int dh = 0; dh < DH; ++dh)
+          for (int row = 3 * RT; row < NS; ++row) qbuf(i, dh)[sw128_offset(row, t)] = 0;
     int it = 0, jc = 0;
     bool aborted = false;
     for (int p = blockIdx.x; !aborted && p < total_jobs; p += gridDim.x) {
@@ -753,50 +796,58 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       const int L = a.seq_lens[seq];
       const int nsp = a.n_splits[seq];
       const int row0 = g * RT + col0;
-      float qv[NQP], qm[NQP];
+      float qv[DH][NQP], qm[DH][NQP];
       const int64_t qbase = (int64_t)seq * q_len * a.q_stride_tok + (int64_t)h * h_r * a.q_stride_head + t;
       auto qoff = [&](int r) {  // element offset of row r's head-dim element t
         const int R = min(row0 + r, n_q - 1);
         return qbase + (int64_t)(R / h_r) * a.q_stride_tok + (int64_t)(R % h_r) * a.q_stride_head;
       };
-      auto moff = [&](int r) { return (int64_t)(h * h_r + min(row0 + r, n_q - 1) % h_r) * 128 + t; };
-      if (a.q_dtype == MJ_DT_BF16) {
-        const __nv_bfloat16* q16 = reinterpret_cast<const __nv_bfloat16*>(a.q);
+      auto moff = [&](int r) { return (int64_t)(h * h_r + min(row0 + r, n_q - 1) % h_r) * D + t; };
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) qv[r] = __bfloat162float(q16[qoff(r)]);
-      } else if (a.q_dtype == MJ_DT_FP16) {
-        const __half* q16 = reinterpret_cast<const __half*>(a.q);
+      for (int dh = 0; dh < DH; ++dh) {  // head-dim elements dh * 128 + t
+        if (a.q_dtype == MJ_DT_BF16) {
+          const __nv_bfloat16* q16 = reinterpret_cast<const __nv_bfloat16*>(a.q) + dh * 128;
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) qv[r] = __half2float(q16[qoff(r)]);
-      } else {
-        const float* q32 = reinterpret_cast<const float*>(a.q);
+          for (int r = 0; r < NQP; ++r) qv[dh][r] = __bfloat162float(q16[qoff(r)]);
+        } else if (a.q_dtype == MJ_DT_FP16) {
+          const __half* q16 = reinterpret_cast<const __half*>(a.q) + dh * 128;
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) qv[r] = q32[qoff(r)];
-      }
-      if (a.q_mul) {
+          for (int r = 0; r < NQP; ++r) qv[dh][r] = __half2float(q16[qoff(r)]);
+        } else {
+          const float* q32 = reinterpret_cast<const float*>(a.q) + dh * 128;
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) qm[r] = a.q_mul[moff(r)];
-      } else {
+          for (int r = 0; r < NQP; ++r) qv[dh][r] = q32[qoff(r)];
+        }
+        if (a.q_mul) {
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) qm[r] = 1.f;
+          for (int r = 0; r < NQP; ++r) qm[dh][r] = a.q_mul[moff(r) + dh * 128];
+        } else {
+#pragma unroll
+          for (int r = 0; r < NQP; ++r) qm[dh][r] = 1.f;
+        }
       }
       float qmax = 0.f;
 #pragma unroll
-      for (int r = 0; r < NQP; ++r) {
-        qv[r] = row0 + r < n_q ? qv[r] * qm[r] : 0.f;
-        qmax = fmaxf(qmax, fabsf(qv[r]));
-      }
+      for (int dh = 0; dh < DH; ++dh)
+#pragma unroll
+        for (int r = 0; r < NQP; ++r) {
+          qv[dh][r] = row0 + r < n_q ? qv[dh][r] * qm[dh][r] : 0.f;
+          qmax = fmaxf(qmax, fabsf(qv[dh][r]));
+        }
       qmax = warp_max_f32(qmax);
       if (lane == 0) red[wq] = qmax;
       if (named_bar_or(bar_id, 128, *abort_flag != 0)) break;
       qmax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
       const float qs = qmax > 0.f ? 224.f / qmax : 1.f;  // |q * qs| <= 224
-      unsigned char* qb = qbuf(jc & 1);
 #pragma unroll
-      for (int r = 0; r < NQP; r += 2) {
-        uint16_t hb, mb, lb;
-        split3(qv[r] * qs, qv[r + 1] * qs, hb, mb, lb);
-        store_split<RT>(qb, col0 + r, t, hb, mb, lb);
+      for (int dh = 0; dh < DH; ++dh) {
+        unsigned char* qb = qbuf(jc & 1, dh);
+#pragma unroll
+        for (int r = 0; r < NQP; r += 2) {
+          uint16_t hb, mb, lb;
+          split3(qv[dh][r] * qs, qv[dh][r + 1] * qs, hb, mb, lb);
+          store_split<RT>(qb, col0 + r, t, hb, mb, lb);
+        }
       }
       fence_proxy_async_smem();
       const float kd = descale_at(a.k_descale, a.k_descale_mode, seq, h, h_k);
@@ -929,15 +980,17 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
             tc_fence_after();
             if constexpr (NWG == 1) {  // the three row blocks are contiguous: 3 * NQP columns
 #pragma unroll
-              for (int c = 0; c < 3 * NQP; c += 8) {
-                float ov[8];
-                tmem_ld8(o_taddr + c, ov);
-                tmem_wait_ld();
+              for (int dh = 0; dh < DH; ++dh)
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                  if (c + k < 3 * NQP) ov[k] *= cc[(c + k) % NQP];
-                tmem_st8(o_taddr + c, ov);
-              }
+                for (int c = 0; c < 3 * NQP; c += 8) {
+                  float ov[8];
+                  tmem_ld8(o_taddr + dh * NO + c, ov);
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int k = 0; k < 8; ++k)
+                    if (c + k < 3 * NQP) ov[k] *= cc[(c + k) % NQP];
+                  tmem_st8(o_taddr + dh * NO + c, ov);
+                }
             } else {  // this warpgroup's NQP columns of each row block
 #pragma unroll
               for (int blk = 0; blk < 3; ++blk)
@@ -1026,17 +1079,19 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       if (!mbar_wait(&b.o_full[(it - 1) & 1], ((it - 1) >> 1) & 1, abort_flag, wait_ns) && !*abort_flag)
         give_up();
       tc_fence_after();
-      float orow[NQP];  // this thread's head-dim element of every row: hi + mid / 16 + lo / 256
+      float orow[DH][NQP];  // this thread's head-dim elements of every row: hi + mid / 16 + lo / 256
 #pragma unroll
-      for (int c = 0; c < NQP; c += 8) {
-        float hv[8], mv[8], lv[8];
-        tmem_ld8(o_taddr + col0 + c, hv);
-        tmem_ld8(o_taddr + RT + col0 + c, mv);
-        tmem_ld8(o_taddr + 2 * RT + col0 + c, lv);
-        tmem_wait_ld();
+      for (int dh = 0; dh < DH; ++dh)
 #pragma unroll
-        for (int k = 0; k < 8 && c + k < NQP; ++k) orow[c + k] = hv[k] + mv[k] * 0.0625f + lv[k] * 0.00390625f;
-      }
+        for (int c = 0; c < NQP; c += 8) {
+          float hv[8], mv[8], lv[8];
+          tmem_ld8(o_taddr + dh * NO + col0 + c, hv);
+          tmem_ld8(o_taddr + dh * NO + RT + col0 + c, mv);
+          tmem_ld8(o_taddr + dh * NO + 2 * RT + col0 + c, lv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 8 && c + k < NQP; ++k) orow[dh][c + k] = hv[k] + mv[k] * 0.0625f + lv[k] * 0.00390625f;
+        }
       tc_fence_before();
       mbar_arrive(b.o_free);  // the next job's first PV may overwrite O
       if (named_bar_or(bar_id, 128, *abort_flag != 0)) {
@@ -1053,35 +1108,39 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
       } else {
         // O rows: normalized, times the V channel scales (final) -- the o_mul
         // reads are issued together, the dtype branch taken once per job
-        float o[NQP];
 #pragma unroll
-        for (int r = 0; r < NQP; ++r) {
-          const float lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
-          o[r] = lt > 0.f ? orow[r] * __fdividef(vscale, lt) : 0.f;
-        }
-        if (final_out && a.o_mul) {
-          float om[NQP];
+        for (int dh = 0; dh < DH; ++dh) {  // head-dim element e = dh * 128 + t
+          const int e = dh * 128 + t;
+          float o[NQP];
 #pragma unroll
-          for (int r = 0; r < NQP; ++r) om[r] = a.o_mul[(int64_t)qh_of(min(r, n_q - 1 - row0)) * 128 + t];
-#pragma unroll
-          for (int r = 0; r < NQP; ++r) o[r] *= om[r];
-        }
-        if (final_out) {
-          if (a.o_dtype == MJ_DT_BF16) {
-            __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(a.o);
-#pragma unroll
-            for (int r = 0; r < NQP; ++r)
-              if (row0 + r < n_q) o16[tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + t] = __float2bfloat16_rn(o[r]);
-          } else {
-#pragma unroll
-            for (int r = 0; r < NQP; ++r)
-              if (row0 + r < n_q) store_elem(a.o, tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + t, a.o_dtype, o[r]);
+          for (int r = 0; r < NQP; ++r) {
+            const float lt = lred[r] + lred[NQP + r] + lred[2 * NQP + r] + lred[3 * NQP + r];
+            o[r] = lt > 0.f ? orow[dh][r] * __fdividef(vscale, lt) : 0.f;
           }
-        } else {
-          const int64_t prow = (((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + row0;
+          if (final_out && a.o_mul) {
+            float om[NQP];
 #pragma unroll
-          for (int r = 0; r < NQP; ++r)
-            if (row0 + r < n_q) a.o_part[(prow + r) * 128 + t] = o[r];
+            for (int r = 0; r < NQP; ++r) om[r] = a.o_mul[(int64_t)qh_of(min(r, n_q - 1 - row0)) * D + e];
+#pragma unroll
+            for (int r = 0; r < NQP; ++r) o[r] *= om[r];
+          }
+          if (final_out) {
+            if (a.o_dtype == MJ_DT_BF16) {
+              __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(a.o);
+#pragma unroll
+              for (int r = 0; r < NQP; ++r)
+                if (row0 + r < n_q) o16[tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + e] = __float2bfloat16_rn(o[r]);
+            } else {
+#pragma unroll
+              for (int r = 0; r < NQP; ++r)
+                if (row0 + r < n_q) store_elem(a.o, tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + e, a.o_dtype, o[r]);
+            }
+          } else {
+            const int64_t prow = (((int64_t)split * a.part_seqs + seq) * h_k + h) * n_q + row0;
+#pragma unroll
+            for (int r = 0; r < NQP; ++r)
+              if (row0 + r < n_q) a.o_part[(prow + r) * D + e] = o[r];
+          }
         }
         if (t < NQP && row0 + t < n_q) {  // LSE (natural log) of row t: thread t writes it
           float lt = 0.f, mr = 0.f;
@@ -1132,22 +1191,28 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW>::THREADS, Cfg<FMT, NQ
               if (row0 + r >= n_q) break;
               float m = -INFINITY;
               for (int k = 0; k < ns; ++k) m = fmaxf(m, lsm[k * NQP + r]);
-              float ov[MAXS];
+              float den = 0.f;
 #pragma unroll
-              for (int k = 0; k < MAXS; ++k) ov[k] = k < ns ? __ldcg(a.o_part + (k * stride + base + r) * 128 + t) : 0.f;
-              float den = 0.f, acc = 0.f;
-              if (m != -INFINITY) {
+              for (int dh = 0; dh < DH; ++dh) {  // head-dim element e = dh * 128 + t
+                const int e = dh * 128 + t;
+                float ov[MAXS];
 #pragma unroll
-                for (int k = 0; k < MAXS; ++k)
-                  if (k < ns) {
-                    const float w = __expf(lsm[k * NQP + r] - m);
-                    den += w;
-                    acc = fmaf(w, ov[k], acc);
-                  }
+                for (int k = 0; k < MAXS; ++k) ov[k] = k < ns ? __ldcg(a.o_part + (k * stride + base + r) * D + e) : 0.f;
+                float acc = 0.f;
+                den = 0.f;
+                if (m != -INFINITY) {
+#pragma unroll
+                  for (int k = 0; k < MAXS; ++k)
+                    if (k < ns) {
+                      const float w = __expf(lsm[k * NQP + r] - m);
+                      den += w;
+                      acc = fmaf(w, ov[k], acc);
+                    }
+                }
+                float o = den > 0.f ? acc / den : 0.f;
+                if (a.o_mul) o *= a.o_mul[(int64_t)qh_of(r) * D + e];
+                store_elem(a.o, tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + e, a.o_dtype, o);
               }
-              float o = den > 0.f ? acc / den : 0.f;
-              if (a.o_mul) o *= a.o_mul[(int64_t)qh_of(r) * 128 + t];
-              store_elem(a.o, tok_of(r) * a.o_stride_tok + qh_of(r) * a.o_stride_head + t, a.o_dtype, o);
               if (t == 0 && a.lse) a.lse[tok_of(r) * a.h_q + qh_of(r)] = den > 0.f ? m + __logf(den) : -INFINITY;
             }
           }
@@ -1180,11 +1245,11 @@ std::mutex& tc_init_mutex();
 // Launch (or, when `dry`, only prepare and check) one tensor-core variant.
 // cudaErrorNotSupported: this variant's register split does not fit the
 // launch allocation on this build; the caller tries the next variant.
-template <int FMT, int NQP, int NWG, int CVTW, bool FUSED>
+template <int FMT, int NQP, int NWG, int CVTW, bool FUSED, int DH = 1>
 static cudaError_t launch_tc_t(const mj_decode_args& a, const CUtensorMap& mk, const CUtensorMap& mv,
                                cudaStream_t stream, bool dry) {
-  using C = tc::Cfg<FMT, NQP, NWG, CVTW>;
-  auto kern = tc::decode_tc_kernel<FMT, NQP, NWG, CVTW, FUSED>;
+  using C = tc::Cfg<FMT, NQP, NWG, CVTW, DH>;
+  auto kern = tc::decode_tc_kernel<FMT, NQP, NWG, CVTW, FUSED, DH>;
   const int smem = C::SMEM;
   static std::atomic<int> slots_of[kMaxDevices];  // resident CTAs per device; 0 unknown, -1 unusable
   int dev = 0;
@@ -1270,10 +1335,28 @@ static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensor
   }
 }
 
+// head_dim 256: one warpgroup of 4, 8 or 16 rows (row groups of 16 beyond),
+// one CTA per SM; narrow formats with a converter warpgroup, fp8 without.
+template <int FMT, bool FUSED>
+static cudaError_t dispatch_fmt_d256(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
+                                     cudaStream_t stream, bool dry) {
+  if constexpr (tc::Fmt<FMT>::SCALED) {
+    return cudaErrorNotSupported;  // nvfp4 at head_dim 256 runs the CUDA-core kernel
+  } else {
+    constexpr int CV = tc::Fmt<FMT>::NARROW ? 1 : 0;
+    if (n_q <= 4) return launch_tc_t<FMT, 4, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
+    if (n_q <= 8) return launch_tc_t<FMT, 8, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
+    return launch_tc_t<FMT, 16, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
+  }
+}
+
 // The entry the host side (decode_tc.cu) calls for one KV format.
 template <int FMT>
 cudaError_t launch_tc_fmt(const mj_decode_args& a, int n_q, bool fused, const CUtensorMap& mk, const CUtensorMap& mv,
                           cudaStream_t stream, bool dry) {
+  if (a.head_size == 256)
+    return fused ? dispatch_fmt_d256<FMT, true>(a, n_q, mk, mv, stream, dry)
+                 : dispatch_fmt_d256<FMT, false>(a, n_q, mk, mv, stream, dry);
   return fused ? dispatch_fmt<FMT, true>(a, n_q, mk, mv, stream, dry)
                : dispatch_fmt<FMT, false>(a, n_q, mk, mv, stream, dry);
 }

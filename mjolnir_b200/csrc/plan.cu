@@ -144,12 +144,15 @@ int mj_plan_split_kv(const int32_t* seq_lens, int num_seqs, int h_k, int n_q_til
 
 // ---- runner handle --------------------------------------------------------
 
+// the tensor-core kernel's rows per job (48; 16 at head_size 256) and CTAs
+// per SM (the configured count up to 16 rows at head_size 128; else one)
 static int runner_n_tiles(const mj_runner* r, int q_len) {
   const int n_q = q_len * (r->h_q / r->h_k);
-  return n_q <= 48 ? 1 : (n_q + 47) / 48;
+  const int rows = r->head_size == 256 ? 16 : 48;
+  return n_q <= rows ? 1 : (n_q + rows - 1) / rows;
 }
 static int runner_ctas(const mj_runner* r, int q_len) {
-  return q_len * (r->h_q / r->h_k) <= 16 ? r->ctas_per_sm : 1;
+  return q_len * (r->h_q / r->h_k) <= 16 && r->head_size == 128 ? r->ctas_per_sm : 1;
 }
 
 void mj_destroy(mj_runner* r) {

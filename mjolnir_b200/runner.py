@@ -307,14 +307,17 @@ class DecodeRunner:
     # ------------------------------------------------------------------ plan
     def n_tiles(self, q_len: int) -> int:
         """CTA jobs per (work item, KV head): the tensor-core kernel serves up to
-        48 query rows per job and cuts larger GQA x draft groups into row groups."""
+        48 query rows per job (16 at head_size 256) and cuts larger GQA x draft
+        groups into row groups."""
         n_q = q_len * self.h_r
-        return 1 if n_q <= 48 else -(-n_q // 48)
+        rows = 16 if self.d == 256 else 48
+        return 1 if n_q <= rows else -(-n_q // rows)
 
     def ctas(self, q_len: int) -> int:
         """Resident CTAs per SM of the kernel variant for this q_len: two for
-        up to 16 query rows per KV head, one (several warpgroups) beyond."""
-        return self.ctas_per_sm if q_len * self.h_r <= 16 else 1
+        up to 16 query rows per KV head, one (several warpgroups, or head_size
+        256) beyond."""
+        return self.ctas_per_sm if q_len * self.h_r <= 16 and self.d == 128 else 1
 
     def slots(self, q_len: int) -> int:
         return max(1, (self.sm_count * self.ctas(q_len)) // (self.h_k * self.n_tiles(q_len)))
@@ -450,7 +453,7 @@ class DecodeRunner:
         launch (the one-warpgroup tensor-core variants given counters), so no
         separate mj_combine launch is needed."""
         return (bool(args.merge_counters) and self.kernel_name(args) == "decode_tc"
-                and args.q_len * (self.h_q // self.h_k) <= 16 and args.max_splits <= 16)
+                and (args.q_len * (self.h_q // self.h_k) <= 16 or self.d == 256) and args.max_splits <= 16)
 
     def run(
         self,

@@ -44,7 +44,7 @@ def test_golden_reference_outputs():
         q = torch.from_numpy(g[name + "__q_bits"]).view(torch.bfloat16).cuda()
         kd = torch.from_numpy(g[name + "__k_descale"]).cuda()
         vd = torch.from_numpy(g[name + "__v_descale"]).cuda()
-        kernels = ["simt"] + (["tc"] if d == 128 and ql * h_q // h_k <= 16 else [])
+        kernels = ["simt"] + (["tc"] if (d == 128 and ql * h_q // h_k <= 16) or d == 256 else [])
         for sm, kernel in [(sm, k) for sm in (148, 2) for k in kernels]:  # 148 SMs: small batches split
             r = DecodeRunner(num_heads=h_q, num_kv_heads=h_k, head_size=d, page_size=PS, max_num_seqs=b,
                              max_q_len=ql, kv_format=fmt, sm_count=sm, kernel=kernel)
@@ -360,3 +360,36 @@ def test_reset_after_an_error_clears_stale_merge_counts():
     ref, _ = c.oracle()
     assert_close_fp32(got.view(c.b, c.h_q, c.d), ref, what="in-kernel merge after a reset")
     assert int(r.merge_counters.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("kv_format,layout", [("fp8", "BHN2D"), ("e2m3", "BHN2D"), ("e3m2", "BHN2D"), ("e2m1", "BHN2D"),
+                                              ("fp8", "B2NHD"), ("e2m3", "2BHND")])
+@pytest.mark.parametrize("q_len,h_q,h_k", [(1, 16, 4), (1, 24, 4), (2, 16, 4), (1, 64, 4), (2, 64, 4)])
+def test_tc_head_dim_256(kv_format, layout, q_len, h_q, h_k):
+    """head_dim 256 on the tensor-core kernel (two 128-wide halves per KV row):
+    4, 6, 8, 16 and 32 query rows per KV head (32: two row groups), the fused
+    K|V box and separate boxes, splits merged by the combine launch and in the
+    kernel, scores that grow along the sequence (the O rescale) and, on the
+    other pass, 1 % of the values x8 (as the decode tests at head_dim 128,
+    one or the other: both together drive |o| to ~20, where the split-fp8
+    operands' relative error meets the 2e-3 absolute bound)."""
+    for fused_merge, seed, ramp, outl in ((False, 61, 2.0, 0.0), (True, 62, 0.0, 0.01)):
+        c = Case(seq_lens=(2100, 700, 129, 33), q_len=q_len, h_q=h_q, h_k=h_k, d=256, kv_format=kv_format,
+                 layout=layout, seed=seed + q_len, k_ramp=ramp, outliers=outl)
+        assert _kernel_of(c, kernel="tc") == "decode_tc"
+        out, _, plan = c.run(kernel="tc", fused_merge=fused_merge)
+        assert plan.with_reduction
+        ref, _ = c.oracle()
+        T = c.b * q_len
+        assert_close_fp32(out[:T].view(T, c.h_q, c.d), ref,
+                          what=f"d256 {kv_format}/{layout} n_q {q_len * h_q // h_k} merge {fused_merge}")
+        assert torch.isnan(out[T:]).all(), "wrote past the batch"
+
+
+def test_tc_head_dim_256_reference_shape_bf16():
+    """The reference harness's own shape (24 q / 4 KV heads, head_dim 256,
+    page 128), bf16 output, one long sequence split across the SMs."""
+    c = Case(seq_lens=(9000,), h_q=24, h_k=4, d=256, page_size=128, kv_format="fp8", layout="BHN2D", seed=70)
+    out, _, plan = c.run(out_dtype=torch.bfloat16, kernel="tc")
+    ref, _ = c.oracle()
+    assert_close_bf16(out[:1].view(1, c.h_q, c.d), ref, what="d256 reference shape")
