@@ -49,6 +49,9 @@ WORKLOADS = {
     "cfg5": dict(h_q=64, h_k=8, d=128, b=256, q_len=1, L=131072, kv="e2m3", PS=16),
     # the north-star target shape: Qwen3-8B e2m3 decode, batch 128 x 32K context
     "ns": dict(h_q=32, h_k=8, d=128, b=128, q_len=1, L=32768, kv="e2m3", PS=16),
+    # the reference harness's own default head shape (24 q / 4 KV heads,
+    # head_dim 256, page 128), batch 16 x 32K
+    "hd256": dict(h_q=24, h_k=4, d=256, b=16, q_len=1, L=32768, kv="fp8", PS=128),
 }
 
 

@@ -53,6 +53,9 @@
 #include "common.cuh"
 #include "sm100.cuh"
 
+#ifndef MJ_D256_SMV
+#define MJ_D256_SMV 1
+#endif
 #ifndef MJ_NVFP4_SMV
 #define MJ_NVFP4_SMV 1
 #endif
@@ -198,6 +201,9 @@ struct Cfg {
   // S MMA's path), the softmax warpgroup converts V after publishing P (ns
   // shape +5 %; at 8 rows the softmax has no room for it: -10 %)
   static constexpr bool SM_CVT_V = MJ_NVFP4_SMV && Fmt<FMT>::SCALED && NWG == 1 && NQP <= 4;
+  // head_dim 256, narrow formats: the converter warpgroup converts V's first
+  // half, the softmax warpgroup the second after publishing P (e2m3 +3.6 %)
+  static constexpr bool SM_CVT_VHI = MJ_D256_SMV && DH == 2 && Fmt<FMT>::NARROW && !Fmt<FMT>::SCALED;
   // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
   // warpgroup w owns rows w * NQP .. of each block.
   static constexpr int NS = (3 * RT + 7) / 8 * 8 < 16 ? 16 : (3 * RT + 7) / 8 * 8;  // S MMA N (Q is K-major)
@@ -385,7 +391,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
       if (i == 0) mbar_init(b.o_free, 128 * NWG);
       // narrow formats: the converter role (and, without a converter
       // warpgroup, the softmax warpgroups) share the V conversion
-      mbar_init(&b.v_ready[i], C::SM_CVT_V ? 128 : Fmt<FMT>::NARROW ? C::CVT_THREADS : C::CVT_ROLE);
+      mbar_init(&b.v_ready[i], C::SM_CVT_V ? 128 : Fmt<FMT>::NARROW ? C::CVT_THREADS + (C::SM_CVT_VHI ? 128 : 0) : C::CVT_ROLE);
       mbar_init(&b.v_free[i], 1);
       mbar_init(&b.q_full[i], NWG);
     }
@@ -521,7 +527,7 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
           // converter warpgroup the softmax warpgroups convert the others
           // after publishing P
 #pragma unroll
-          for (int dh = 0; dh < DH; ++dh) {
+          for (int dh = 0; dh < (C::SM_CVT_VHI ? 1 : DH); ++dh) {
             unsigned char* vb = vbuf(st, dh);
 #pragma unroll 2
             for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
@@ -1053,6 +1059,17 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
           unsigned char* vb = vbuf(st);
 #pragma unroll 2
           for (int c = C::CVT_ROLE + sw * 128 + t; c < kTileBytes / 16; c += C::CVT_THREADS) {
+            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+            *q = Fmt<FMT>::convert(*q);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&b.v_ready[it & 1]);
+        } else if constexpr (C::SM_CVT_VHI) {  // head_dim 256: the second half of this tile's V
+          const int st = it % S;
+          if (!FUSED && !mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, wait_ns) && !*abort_flag) give_up();
+          unsigned char* vb = vbuf(st, 1);
+#pragma unroll 2
+          for (int c = t; c < kTileBytes / 16; c += 128) {
             uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
             *q = Fmt<FMT>::convert(*q);
           }
