@@ -55,7 +55,6 @@ const char* tc_ineligible(const mj_decode_args& a) {
       if (ss[i] % 8) return "nvfp4 scale stride alignment";
   }
   if (a.head_size != 128 && a.head_size != 256) return "head_size not 128 or 256";
-  if (a.head_size == 256 && a.kv_format == MJ_KV_NVFP4) return "nvfp4 at head_size 256";
   if (a.page_size != 16 && a.page_size != 32 && a.page_size != 64 && a.page_size != 128) return "page size";
   if (a.num_pages >= (int64_t)INT32_MAX) return "num_pages";
   const uintptr_t al = a.kv_format == MJ_KV_FP8_E4M3 ? 16 : 32;

@@ -185,7 +185,7 @@ struct Fmt {
 // thread owns head-dim elements t and 128 + t; one CTA per SM.
 template <int FMT, int NQP, int NWG, int CVTW, int DH = 1>
 struct Cfg {
-  static_assert(DH == 1 || (DH == 2 && NWG == 1 && !Fmt<FMT>::SCALED), "head_dim 256: one warpgroup, no nvfp4");
+  static_assert(DH == 1 || (DH == 2 && NWG == 1), "head_dim 256: one warpgroup");
   static constexpr int RT = NWG * NQP;
   static constexpr int SM0 = 4 * (1 + CVTW);             // first softmax warp
   static constexpr int THREADS = 128 * (1 + CVTW + NWG);
@@ -200,7 +200,7 @@ struct Cfg {
   // nvfp4 at 4 rows per KV head: the converter warpgroup converts K (on the
   // S MMA's path), the softmax warpgroup converts V after publishing P (ns
   // shape +5 %; at 8 rows the softmax has no room for it: -10 %)
-  static constexpr bool SM_CVT_V = MJ_NVFP4_SMV && Fmt<FMT>::SCALED && NWG == 1 && NQP <= 4;
+  static constexpr bool SM_CVT_V = MJ_NVFP4_SMV && Fmt<FMT>::SCALED && NWG == 1 && NQP <= 4 && DH == 1;
   // head_dim 256, narrow formats: the converter warpgroup converts V's first
   // half, the softmax warpgroup the second after publishing P (e2m3 +3.6 %)
   static constexpr bool SM_CVT_VHI = MJ_D256_SMV && DH == 2 && Fmt<FMT>::NARROW && !Fmt<FMT>::SCALED;
@@ -211,7 +211,7 @@ struct Cfg {
   static constexpr int QBYTES = NS * 128;                // one K-major Q operand
   static constexpr int PBYTES = NO * 128;                // one MN-major P operand: NO/16 groups of [128 s][16 B]
   // (nvfp4 at 8 rows: its scale copies leave room for two stages at two CTAs per SM)
-  static constexpr int STAGES = DH == 2 ? (NQP <= 8 ? 3 : 2)
+  static constexpr int STAGES = DH == 2 ? (NQP <= 8 && !Fmt<FMT>::SCALED ? 3 : 2)
                                : NWG == 1 ? (NQP <= 4 || (NQP == 8 && !Fmt<FMT>::SCALED) ? 3 : 2) : NWG == 2 ? 5 : 4;
   static_assert(DH == 1 || !SM_CONVERTS, "head_dim 256: narrow formats convert on a converter warpgroup");
   static_assert(!Fmt<FMT>::SCALED || CVTW == 1, "nvfp4 converts K on the converter warpgroup only");
@@ -240,7 +240,7 @@ struct Cfg {
   static constexpr int MISC_OFF = RED_OFF + NWG * 2 * 4 * NQP * 4;  // tmem base, abort, never_abort, l scratch [NWG][4][NQP]
   // nvfp4: per stage the K then V scale rows of the tile ([128 rows][8 B] each)
   static constexpr int SC_OFF = (MISC_OFF + 64 + NWG * 4 * 4 * NQP + 15) / 16 * 16;
-  static constexpr int SC_BYTES = Fmt<FMT>::SCALED ? STAGES * 2 * 128 * 8 : 0;
+  static constexpr int SC_BYTES = Fmt<FMT>::SCALED ? STAGES * DH * 2 * 128 * 8 : 0;  // per half: 8 B a row
   // nvfp4: for each of the 256 scale bytes the e4m3 bytes of the 8 code magnitudes
   static constexpr int LUT_OFF = SC_OFF + SC_BYTES;
   static constexpr int SMEM = LUT_OFF + (Fmt<FMT>::SCALED ? 256 * 8 : 0);
@@ -447,8 +447,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
   // byte offset of 16-byte chunk c (row c / 8) of the V tile, and of row r
   auto vchunk = [&](int c) { return (uint32_t)((c >> 6) * ATOM + (c & 63) * 16); };
   auto qbuf = [&](int i, int dh = 0) { return sm + C::Q_OFF + (i * DH + dh) * C::QBYTES; };
-  auto kscl = [&](int st) { return sm + C::SC_OFF + st * 2048; };  // nvfp4 K scale rows of a stage
-  auto vscl = [&](int st) { return sm + C::SC_OFF + st * 2048 + 1024; };
+  // nvfp4 K / V scale rows of a stage (and head-dim half): [128 rows][8 B]
+  auto kscl = [&](int st, int dh = 0) { return sm + C::SC_OFF + (st * DH + dh) * 2048; };
+  auto vscl = [&](int st, int dh = 0) { return sm + C::SC_OFF + (st * DH + dh) * 2048 + 1024; };
   auto pbuf = [&](int i) { return sm + C::P_OFF + i * C::PBYTES; };
   auto give_up = [&]() {
     *abort_flag = 1;
@@ -505,14 +506,16 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
           const int valid = L - tile * kTileRows;
           ok = mbar_wait(&b.k_full[st], (it / S) & 1, abort_flag, wait_ns);
           if (!ok) break;
-          nvfp4_tile(kbuf(st), kscl(st), valid, ct, C::CVT_ROLE);
+#pragma unroll
+          for (int dh = 0; dh < DH; ++dh) nvfp4_tile(kbuf(st, dh), kscl(st, dh), valid, ct, C::CVT_ROLE);
           fence_proxy_async_smem();
           mbar_arrive(&b.k_ready[st]);
           if constexpr (C::SM_CVT_V) continue;
           ok = (FUSED || mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, wait_ns)) &&
                mbar_wait(&b.v_free[it & 1], ((it >> 1) & 1) ^ 1, abort_flag, wait_ns);
           if (!ok) break;
-          nvfp4_tile(vbuf(st), vscl(st), valid, ct, C::CVT_ROLE);
+#pragma unroll
+          for (int dh = 0; dh < DH; ++dh) nvfp4_tile(vbuf(st, dh), vscl(st, dh), valid, ct, C::CVT_ROLE);
           fence_proxy_async_smem();
           mbar_arrive(&b.v_ready[it & 1]);
           continue;
@@ -601,13 +604,16 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
           const unsigned char* base = reinterpret_cast<const unsigned char*>(v ? a.v_scales : a.k_scales);
           const int64_t sp = v ? a.vs_stride_page : a.ks_stride_page, sr = v ? a.vs_stride_row : a.ks_stride_row;
           const int64_t sh = v ? a.vs_stride_head : a.ks_stride_head;
-          unsigned char* dst = v ? vscl(st) : kscl(st);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int r = lane + 32 * i;
             const int pr = __shfl_sync(0xffffffffu, pg, r / PS);
-            if (r < valid && pr < a.num_pages)
-              cp_async8(dst + r * 8, base + (int64_t)pr * sp + (int64_t)(r % PS) * sr + (int64_t)h * sh);
+            if (r < valid && pr < a.num_pages) {
+              const unsigned char* src = base + (int64_t)pr * sp + (int64_t)(r % PS) * sr + (int64_t)h * sh;
+#pragma unroll
+              for (int dh = 0; dh < DH; ++dh)  // head_dim 256: 16 scale bytes a row, 8 per half
+                cp_async8((v ? vscl(st, dh) : kscl(st, dh)) + r * 8, src + dh * 8);
+            }
           }
         };
         // one tile into stage it % S once the stage is free; false on give-up
@@ -1353,18 +1359,15 @@ static cudaError_t dispatch_fmt(const mj_decode_args& a, int n_q, const CUtensor
 }
 
 // head_dim 256: one warpgroup of 4, 8 or 16 rows (row groups of 16 beyond),
-// one CTA per SM; narrow formats with a converter warpgroup, fp8 without.
+// one CTA per SM; narrow formats (nvfp4 included) with a converter
+// warpgroup, fp8 without.
 template <int FMT, bool FUSED>
 static cudaError_t dispatch_fmt_d256(const mj_decode_args& a, int n_q, const CUtensorMap& mk, const CUtensorMap& mv,
                                      cudaStream_t stream, bool dry) {
-  if constexpr (tc::Fmt<FMT>::SCALED) {
-    return cudaErrorNotSupported;  // nvfp4 at head_dim 256 runs the CUDA-core kernel
-  } else {
-    constexpr int CV = tc::Fmt<FMT>::NARROW ? 1 : 0;
-    if (n_q <= 4) return launch_tc_t<FMT, 4, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
-    if (n_q <= 8) return launch_tc_t<FMT, 8, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
-    return launch_tc_t<FMT, 16, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
-  }
+  constexpr int CV = tc::Fmt<FMT>::NARROW ? 1 : 0;
+  if (n_q <= 4) return launch_tc_t<FMT, 4, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
+  if (n_q <= 8) return launch_tc_t<FMT, 8, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
+  return launch_tc_t<FMT, 16, 1, CV, FUSED, 2>(a, mk, mv, stream, dry);
 }
 
 // The entry the host side (decode_tc.cu) calls for one KV format.

@@ -64,7 +64,7 @@ def _kernel_of(c, **kw):
     plan = r.plan(c.seq_lens, c.b, c.q_len, c.block_table, c.seq_lens_t)
     out = torch.empty(c.b * c.q_len, c.h_q * c.d, device="cuda")
     args = r.decode_args(plan, c.query, out, c.k_view, c.v_view, c.dev(c.kd), c.dev(c.vd), 0.1,
-                         q_mul=c.dev(c.q_mul), o_mul=c.dev(c.o_mul))
+                         q_mul=c.dev(c.q_mul), o_mul=c.dev(c.o_mul), k_scales=c.k_scales, v_scales=c.v_scales)
     return _lib.KERNEL_NAMES[_lib.decode_kernel(args)]
 
 
@@ -363,7 +363,7 @@ def test_reset_after_an_error_clears_stale_merge_counts():
 
 
 @pytest.mark.parametrize("kv_format,layout", [("fp8", "BHN2D"), ("e2m3", "BHN2D"), ("e3m2", "BHN2D"), ("e2m1", "BHN2D"),
-                                              ("fp8", "B2NHD"), ("e2m3", "2BHND")])
+                                              ("nvfp4", "BHN2D"), ("fp8", "B2NHD"), ("e2m3", "2BHND"), ("nvfp4", "B2NHD")])
 @pytest.mark.parametrize("q_len,h_q,h_k", [(1, 16, 4), (1, 24, 4), (2, 16, 4), (1, 64, 4), (2, 64, 4)])
 def test_tc_head_dim_256(kv_format, layout, q_len, h_q, h_k):
     """head_dim 256 on the tensor-core kernel (two 128-wide halves per KV row):
