@@ -81,7 +81,7 @@ extern "C" {
 #define MJ_DT_FP32 2
 
 /* decode kernels: AUTO picks the tensor-core kernel when it can run the
- * arguments (head_size 128, page 16..128, TMA-aligned KV views), else the
+ * arguments (head_size 128 or 256, page 16..128, TMA-aligned KV views), else the
  * CUDA-core kernel; TC demands the former. */
 #define MJ_KERNEL_AUTO 0
 #define MJ_KERNEL_SIMT 1
