@@ -6,7 +6,8 @@ a 2-layer Qwen3-shaped model with random weights generates on an fp8 cache
 with calibration on (the decode steps on the kernel, the prefill on the
 FlashInfer fallback), then on the packed fp6_e2m3 cache with the scales that
 calibration wrote (kernel decode, fallback prefill on the expanded e4m3
-scratch). Each run is its own process.
+scratch). Each run is its own process. Both head sizes the kernel takes:
+head_dim 128 (Qwen3's) and 256.
 """
 
 import importlib.util
@@ -45,10 +46,11 @@ CONFIG = {
 
 @pytest.mark.skipif(importlib.util.find_spec("vllm") is None or os.environ.get("MJOLNIR_VLLM_E2E") == "0",
                     reason="needs vLLM (and MJOLNIR_VLLM_E2E not 0)")
-def test_vllm_generates_on_the_kernel(tmp_path):
+@pytest.mark.parametrize("head_dim", [128, 256])
+def test_vllm_generates_on_the_kernel(tmp_path, head_dim):
     model = tmp_path / "qwen3-tiny"
     model.mkdir()
-    (model / "config.json").write_text(json.dumps(CONFIG))
+    (model / "config.json").write_text(json.dumps(dict(CONFIG, head_dim=head_dim)))
     scales = tmp_path / "scales.json"
     results = {}
     for kv, calibrate in (("fp8", "1"), ("fp6_e2m3", "0")):
