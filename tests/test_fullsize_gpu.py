@@ -1,5 +1,6 @@
-"""Parity at the benchmark's full sizes (BASELINE configs 2-5 and the
-north-star shape), through the public API: one whole step (cache write of the
+"""Parity at the benchmark's full sizes (the
+north-star shape and the reference harness's head_dim-256 shape), through
+the public API: one whole step (cache write of the
 step's tokens, decode, split merge) over the full resident workload, then
 the oracle on a sample of it -- a few sequences, each with a couple of KV
 heads, dequantised from the very bytes the write kernel left in the cache.
@@ -56,7 +57,8 @@ def _sampled_reference(wl, seqs, heads):
 
 
 @pytest.mark.parametrize("workload,kv", [("cfg2", "fp8"), ("cfg3", "e2m3"), ("ns", "e2m3"), ("cfg4", "e2m3"),
-                                         ("cfg5", "e2m3"), ("cfg5", "fp8"), ("ns", "e3m2"), ("ns", "e2m1"), ("ns", "nvfp4")])
+                                         ("cfg5", "e2m3"), ("cfg5", "fp8"), ("ns", "e3m2"), ("ns", "e2m1"), ("ns", "nvfp4"),
+                                         ("hd256", "fp8"), ("hd256", "e2m3"), ("hd256", "nvfp4")])
 def test_full_size_step_sampled_parity(workload, kv):
     import bench
 
