@@ -56,6 +56,9 @@
 #ifndef MJ_D256_SMV
 #define MJ_D256_SMV 1
 #endif
+#ifndef MJ_D256_SM_CHUNKS
+#define MJ_D256_SM_CHUNKS 512
+#endif
 #ifndef MJ_NVFP4_SMV
 #define MJ_NVFP4_SMV 1
 #endif
@@ -201,9 +204,13 @@ struct Cfg {
   // S MMA's path), the softmax warpgroup converts V after publishing P (ns
   // shape +5 %; at 8 rows the softmax has no room for it: -10 %)
   static constexpr bool SM_CVT_V = MJ_NVFP4_SMV && Fmt<FMT>::SCALED && NWG == 1 && NQP <= 4 && DH == 1;
-  // head_dim 256, narrow formats: the converter warpgroup converts V's first
-  // half, the softmax warpgroup the second after publishing P (e2m3 +3.6 %)
+  // head_dim 256, narrow formats: the softmax warpgroup converts part of the
+  // V tile after publishing P, the converter warpgroup the rest
   static constexpr bool SM_CVT_VHI = MJ_D256_SMV && DH == 2 && Fmt<FMT>::NARROW && !Fmt<FMT>::SCALED;
+  // of the 2 x 1024 16-byte chunks of such a V tile: the last SM_CHUNKS to the
+  // softmax warpgroup, the others to the converter warpgroup (at the
+  // reference's head shape, e2m3: none 0.186 ms, 1024 0.181, 512 0.168, 256 0.174)
+  static constexpr int SM_CHUNKS = SM_CVT_VHI ? MJ_D256_SM_CHUNKS : 0;
   // Query rows enter the MMAs as three row blocks (hi, mid, lo) of RT rows;
   // warpgroup w owns rows w * NQP .. of each block.
   static constexpr int NS = (3 * RT + 7) / 8 * 8 < 16 ? 16 : (3 * RT + 7) / 8 * 8;  // S MMA N (Q is K-major)
@@ -529,13 +536,21 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
           // this role converts chunks ct, ct + CVT_THREADS, ...; without a
           // converter warpgroup the softmax warpgroups convert the others
           // after publishing P
-#pragma unroll
-          for (int dh = 0; dh < (C::SM_CVT_VHI ? 1 : DH); ++dh) {
-            unsigned char* vb = vbuf(st, dh);
+          if constexpr (C::SM_CVT_VHI) {  // chunk g of the tile: half g / 1024, chunk g % 1024
 #pragma unroll 2
-            for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
-              uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+            for (int g = ct; g < DH * (kTileBytes / 16) - C::SM_CHUNKS; g += C::CVT_THREADS) {
+              uint4* q = reinterpret_cast<uint4*>(vbuf(st, g >> 10) + vchunk(g & 1023));
               *q = Fmt<FMT>::convert(*q);
+            }
+          } else {
+#pragma unroll
+            for (int dh = 0; dh < DH; ++dh) {
+              unsigned char* vb = vbuf(st, dh);
+#pragma unroll 2
+              for (int c = ct; c < kTileBytes / 16; c += C::CVT_THREADS) {
+                uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+                *q = Fmt<FMT>::convert(*q);
+              }
             }
           }
           // narrow formats have no NaN code: rows past the sequence end are finite and get P = 0
@@ -1073,10 +1088,9 @@ __global__ void __launch_bounds__(Cfg<FMT, NQP, NWG, CVTW, DH>::THREADS, Cfg<FMT
         } else if constexpr (C::SM_CVT_VHI) {  // head_dim 256: the second half of this tile's V
           const int st = it % S;
           if (!FUSED && !mbar_wait(&b.v_full[st], (it / S) & 1, abort_flag, wait_ns) && !*abort_flag) give_up();
-          unsigned char* vb = vbuf(st, 1);
 #pragma unroll 2
-          for (int c = t; c < kTileBytes / 16; c += 128) {
-            uint4* q = reinterpret_cast<uint4*>(vb + vchunk(c));
+          for (int g = DH * (kTileBytes / 16) - C::SM_CHUNKS + t; g < DH * (kTileBytes / 16); g += 128) {
+            uint4* q = reinterpret_cast<uint4*>(vbuf(st, g >> 10) + vchunk(g & 1023));
             *q = Fmt<FMT>::convert(*q);
           }
           fence_proxy_async_smem();
